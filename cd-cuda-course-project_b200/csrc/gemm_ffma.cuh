@@ -1,0 +1,184 @@
+// gemm_ffma.cuh — exact fp32 SIMT GEMM (FFMA), for sm_100a.
+//
+// C = A·B (B row-major K×N) or, with transpose_b, C = A·Bt^T (B holds Bt,
+// row-major N×K). This is the reference `matmul_opt` template
+// (src/generator.py:40-70, B loads at :286-299) restated as a
+// register-blocked kernel: the reference computes one output per thread from
+// T×T shared tiles (one FMA per two shared loads); here each of 256 threads
+// owns an 8×8 block of a 128×128 CTA tile, so every k step does 64 FMAs for
+// four 128-bit shared loads. Tiles are double-buffered through registers
+// (one __syncthreads per k tile). Accumulation order per output is k-ascending
+// fp32 FMA, like the reference's inner loop.
+#pragma once
+#include "kt_common.cuh"
+
+#ifndef KT_FFMA_BK
+#define KT_FFMA_BK 16
+#endif
+#ifndef KT_FFMA_MINB
+#define KT_FFMA_MINB 2
+#endif
+
+namespace kt {
+namespace gemm_ffma {
+
+constexpr int BM = 128, BN = 128, THREADS = 256;
+constexpr int PAD = 4;  // row padding of the k-major shared tiles (bank spread)
+
+// Load 4 consecutive elements along the contiguous dim of a row-major matrix
+// (rows × cols, leading dim ld), zero outside. VEC: 16-byte aligned path.
+template <bool VEC>
+__device__ __forceinline__ float4 load4(const float* __restrict__ p, int64_t row, int64_t col, int64_t rows,
+                                        int64_t cols, int64_t ld) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (row >= rows) return v;
+  const float* q = p + row * ld + col;
+  if (VEC) {
+    if (col + 3 < cols) return __ldg(reinterpret_cast<const float4*>(q));
+  }
+  if (col + 0 < cols) v.x = __ldg(q + 0);
+  if (col + 1 < cols) v.y = __ldg(q + 1);
+  if (col + 2 < cols) v.z = __ldg(q + 2);
+  if (col + 3 < cols) v.w = __ldg(q + 3);
+  return v;
+}
+
+template <bool TB, bool VEC, int BK, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB)
+sgemm_128x128(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int64_t M,
+              int64_t N, int64_t K) {
+  static_assert(BK == 8 || BK == 16 || BK == 32, "BK");
+  // k-major tiles: As[k][m], Bs[k][n]
+  __shared__ __align__(16) float As[2][BK][BM + PAD];
+  __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+  constexpr int AV = BM * BK / 4 / THREADS;  // float4 per thread for a row-major-along-k tile
+  constexpr int BV = BN * BK / 4 / THREADS;  // float4 per thread for a k-rows tile
+  static_assert(AV >= 1 && BV >= 1, "tile/threads");
+  constexpr int KQ = BK / 4;                  // float4 per tile row along k
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+
+  float4 ra[AV], rb[BV];
+  auto load_tile = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < AV; ++i) {
+      const int e = tid + i * THREADS;
+      const int r = e / KQ, kq = (e % KQ) * 4;
+      ra[i] = load4<VEC>(A, m0 + r, k0 + kq, M, K, K);
+    }
+#pragma unroll
+    for (int i = 0; i < BV; ++i) {
+      const int e = tid + i * THREADS;
+      if (TB) {
+        const int r = e / KQ, kq = (e % KQ) * 4;
+        rb[i] = load4<VEC>(B, n0 + r, k0 + kq, N, K, K);
+      } else {
+        const int kr = e / (BN / 4), nq = (e % (BN / 4)) * 4;
+        rb[i] = load4<VEC>(B, k0 + kr, n0 + nq, K, N, N);
+      }
+    }
+  };
+  auto store_tile = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < AV; ++i) {
+      const int e = tid + i * THREADS;
+      const int r = e / KQ, kq = (e % KQ) * 4;
+      As[buf][kq + 0][r] = ra[i].x;
+      As[buf][kq + 1][r] = ra[i].y;
+      As[buf][kq + 2][r] = ra[i].z;
+      As[buf][kq + 3][r] = ra[i].w;
+    }
+#pragma unroll
+    for (int i = 0; i < BV; ++i) {
+      const int e = tid + i * THREADS;
+      if (TB) {
+        const int r = e / KQ, kq = (e % KQ) * 4;
+        Bs[buf][kq + 0][r] = rb[i].x;
+        Bs[buf][kq + 1][r] = rb[i].y;
+        Bs[buf][kq + 2][r] = rb[i].z;
+        Bs[buf][kq + 3][r] = rb[i].w;
+      } else {
+        const int kr = e / (BN / 4), nq = (e % (BN / 4)) * 4;
+        *reinterpret_cast<float4*>(&Bs[buf][kr][nq]) = rb[i];
+      }
+    }
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  const int64_t nk = (K + BK - 1) / BK;
+  load_tile(0);
+  store_tile(0);
+  __syncthreads();
+  for (int64_t t = 0; t < nk; ++t) {
+    const int cur = (int)(t & 1);
+    if (t + 1 < nk) load_tile((t + 1) * BK);
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4 + 64]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4 + 64]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (t + 1 < nk) store_tile(cur ^ 1);
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (row >= M) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t col = n0 + h * 64 + tx * 4;
+      float* c = C + row * N + col;
+      const float4 v = make_float4(acc[i][h * 4 + 0], acc[i][h * 4 + 1], acc[i][h * 4 + 2], acc[i][h * 4 + 3]);
+      if (VEC && col + 3 < N) {
+        *reinterpret_cast<float4*>(c) = v;
+      } else {
+        if (col + 0 < N) c[0] = v.x;
+        if (col + 1 < N) c[1] = v.y;
+        if (col + 2 < N) c[2] = v.z;
+        if (col + 3 < N) c[3] = v.w;
+      }
+    }
+  }
+}
+
+template <bool TB, bool VEC>
+inline void launch_t(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+  sgemm_128x128<TB, VEC, KT_FFMA_BK, KT_FFMA_MINB><<<grid, THREADS, 0, st>>>(A, B, C, M, N, K);
+}
+
+inline int launch(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int tb,
+                  cudaStream_t st) {
+  if (M < 0 || N < 0 || K < 0) return fail(KT_ERR_ARG, "gemm: negative shape");
+  if (M == 0 || N == 0) return KT_OK;
+  if (!A || !B || !C) return fail(KT_ERR_ARG, "gemm: null pointer");
+  if ((M + BM - 1) / BM > 65535) return fail(KT_ERR_UNSUPPORTED, "gemm: M too large for the grid");
+  const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && (K % 4 == 0) && (tb ? true : (N % 4 == 0)) &&
+                   (N % 4 == 0);
+  if (tb) {
+    if (vec) launch_t<true, true>(A, B, C, M, N, K, st);
+    else launch_t<true, false>(A, B, C, M, N, K, st);
+  } else {
+    if (vec) launch_t<false, true>(A, B, C, M, N, K, st);
+    else launch_t<false, false>(A, B, C, M, N, K, st);
+  }
+  return check_launch("gemm ffma");
+}
+
+}  // namespace gemm_ffma
+}  // namespace kt

@@ -1,0 +1,277 @@
+// kt_entry.cuh — the extern "C" surface of one built library.
+//
+// A translation unit defines the template parameters it wants (or takes the
+// defaults), optionally restricts the families it builds with KT_ONLY_<FAM>,
+// and includes this file once. The default library (libkt.cu) builds every
+// family; a generated tuning variant builds one family, and the entry points
+// of the others return KT_ERR_UNSUPPORTED. Every build exports the same
+// symbols, declared in include/kt_abi.h.
+#pragma once
+
+#include <vector>
+
+#include "kt_common.cuh"
+
+#if defined(KT_ONLY_SOFTMAX) || defined(KT_ONLY_LAYERNORM) || defined(KT_ONLY_REDUCE) || \
+    defined(KT_ONLY_GEMM) || defined(KT_ONLY_FA)
+#define KT_SELECTIVE 1
+#else
+#define KT_SELECTIVE 0
+#endif
+
+#if !KT_SELECTIVE || defined(KT_ONLY_SOFTMAX)
+#define KT_WITH_SOFTMAX 1
+#include "softmax.cuh"
+#else
+#define KT_WITH_SOFTMAX 0
+#endif
+#if !KT_SELECTIVE || defined(KT_ONLY_LAYERNORM)
+#define KT_WITH_LAYERNORM 1
+#include "layernorm.cuh"
+#else
+#define KT_WITH_LAYERNORM 0
+#endif
+#if !KT_SELECTIVE || defined(KT_ONLY_REDUCE)
+#define KT_WITH_REDUCE 1
+#include "reduce.cuh"
+#else
+#define KT_WITH_REDUCE 0
+#endif
+#if !KT_SELECTIVE || defined(KT_ONLY_GEMM)
+#define KT_WITH_GEMM 1
+#include "gemm_ffma.cuh"
+#include "gemm_tf32.cuh"
+#else
+#define KT_WITH_GEMM 0
+#endif
+#if !KT_SELECTIVE || defined(KT_ONLY_FA)
+#define KT_WITH_FA 1
+#include "fa_fwd.cuh"
+#else
+#define KT_WITH_FA 0
+#endif
+#include "naive.cuh"
+
+#define KT_STR2(x) #x
+#define KT_STR(x) KT_STR2(x)
+
+#ifndef KT_VARIANT_JSON
+#define KT_VARIANT_JSON "{\"variant\": \"default\"}"
+#endif
+
+// Device error word shared by every kernel of this library that has bounded waits.
+__device__ int g_kt_device_error = 0;
+
+namespace kt {
+
+static thread_local char g_last_error[512] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+static int unsupported(const char* what) {
+  return fail(KT_ERR_UNSUPPORTED, "%s is not built into this library variant", what);
+}
+
+// Evicts L2 between timing samples by streaming the flush buffer through it
+// with loads (clean lines: no write-back traffic lands on the next sample).
+__global__ void flush_l2_kernel(const float4* __restrict__ buf, int64_t n4, float* __restrict__ sink) {
+  float acc = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = buf[i];
+    acc += v.x + v.y + v.z + v.w;
+  }
+  if (acc == 1.2345678e30f) *sink = acc;  // keeps the loads; practically never taken
+}
+
+static int flush_l2(void* flush, size_t bytes, cudaStream_t st) {
+  if (flush == nullptr || bytes < 16) return KT_OK;
+  const int64_t n4 = (int64_t)(bytes / 16);
+  flush_l2_kernel<<<sm_count() * 4, 512, 0, st>>>(static_cast<const float4*>(flush), n4, static_cast<float*>(flush));
+  return check_launch("flush_l2");
+}
+
+}  // namespace kt
+
+extern "C" {
+
+const char* kt_last_error(void) { return kt::g_last_error; }
+
+int kt_version(void) { return KT_ABI_VERSION; }
+
+const char* kt_variant_params(void) { return KT_VARIANT_JSON; }
+
+int kt_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kt_stream_t stream) {
+  kt::clear_error();
+#if KT_WITH_SOFTMAX
+  return kt::softmax::launch(x, y, rows, cols, stream);
+#else
+  return kt::unsupported("softmax");
+#endif
+}
+
+int kt_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y, int64_t rows, int64_t cols,
+                     float eps, kt_stream_t stream) {
+  kt::clear_error();
+#if KT_WITH_LAYERNORM
+  return kt::layernorm::launch(x, gamma, beta, y, rows, cols, eps, stream);
+#else
+  return kt::unsupported("layernorm");
+#endif
+}
+
+size_t kt_reduce_workspace_bytes(int64_t n) {
+#if KT_WITH_REDUCE
+  return kt::reduce::workspace_bytes(n < 0 ? 0 : n);
+#else
+  (void)n;
+  return 0;
+#endif
+}
+
+int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32, void* workspace, size_t ws_bytes,
+                      kt_stream_t stream) {
+  kt::clear_error();
+#if KT_WITH_REDUCE
+  return kt::reduce::launch(x, n, out64, out32, workspace, ws_bytes, stream);
+#else
+  return kt::unsupported("reduce");
+#endif
+}
+
+int kt_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int transpose_b,
+                int variant, kt_stream_t stream) {
+  kt::clear_error();
+#if KT_WITH_GEMM
+  if (variant == KT_GEMM_FFMA) return kt::gemm_ffma::launch(A, B, C, M, N, K, transpose_b, stream);
+  if (variant == KT_GEMM_TF32) return kt::gemm_tf32::launch(A, B, C, M, N, K, transpose_b, &g_kt_device_error, stream);
+  return kt::fail(KT_ERR_ARG, "gemm: unknown variant %d", variant);
+#else
+  return kt::unsupported("gemm");
+#endif
+}
+
+int kt_fa_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int64_t B, int64_t H,
+                   int64_t S, int64_t D, float scale, int causal, kt_stream_t stream) {
+  kt::clear_error();
+#if KT_WITH_FA
+  return kt::fa::launch(Q, K, V, O, B, H, S, D, scale, causal, &g_kt_device_error, stream);
+#else
+  return kt::unsupported("flash-attention forward");
+#endif
+}
+
+int kt_naive_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kt_stream_t stream) {
+  kt::clear_error();
+  return kt::naive::softmax(x, y, rows, cols, stream);
+}
+
+int kt_naive_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y, int64_t rows,
+                           int64_t cols, float eps, kt_stream_t stream) {
+  kt::clear_error();
+  return kt::naive::layernorm(x, gamma, beta, y, rows, cols, eps, stream);
+}
+
+int kt_naive_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32, void* workspace,
+                            size_t ws_bytes, kt_stream_t stream) {
+  kt::clear_error();
+  return kt::naive::reduce(x, n, out64, out32, workspace, ws_bytes, stream);
+}
+
+int kt_naive_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int transpose_b,
+                      kt_stream_t stream) {
+  kt::clear_error();
+  return kt::naive::gemm(A, B, C, M, N, K, transpose_b, stream);
+}
+
+int kt_naive_attention_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int64_t B,
+                            int64_t H, int64_t S, int64_t D, float scale, int causal, kt_stream_t stream) {
+  kt::clear_error();
+  return kt::naive::attention(Q, K, V, O, B, H, S, D, scale, causal, stream);
+}
+
+int kt_run(int op, const kt_args* a, kt_stream_t s) {
+  if (a == nullptr) return kt::fail(KT_ERR_ARG, "kt_run: null args");
+  switch (op) {
+    case KT_OP_SOFTMAX:
+      return kt_softmax_f32((const float*)a->in0, (float*)a->out0, a->d0, a->d1, s);
+    case KT_OP_LAYERNORM:
+      return kt_layernorm_f32((const float*)a->in0, (const float*)a->in1, (const float*)a->in2, (float*)a->out0,
+                              a->d0, a->d1, a->f0, s);
+    case KT_OP_REDUCE:
+      return kt_reduce_sum_f32((const float*)a->in0, a->d0, (double*)a->out0, (float*)a->out1, a->workspace,
+                               a->ws_bytes, s);
+    case KT_OP_GEMM:
+      return kt_gemm_f32((const float*)a->in0, (const float*)a->in1, (float*)a->out0, a->d0, a->d1, a->d2, a->i0,
+                         a->i1, s);
+    case KT_OP_FA_FWD:
+      return kt_fa_fwd_bf16((const uint16_t*)a->in0, (const uint16_t*)a->in1, (const uint16_t*)a->in2,
+                            (uint16_t*)a->out0, a->d0, a->d1, a->d2, a->d3, a->f0, a->i0, s);
+    case KT_OP_NAIVE_SOFTMAX:
+      return kt_naive_softmax_f32((const float*)a->in0, (float*)a->out0, a->d0, a->d1, s);
+    case KT_OP_NAIVE_LAYERNORM:
+      return kt_naive_layernorm_f32((const float*)a->in0, (const float*)a->in1, (const float*)a->in2,
+                                    (float*)a->out0, a->d0, a->d1, a->f0, s);
+    case KT_OP_NAIVE_REDUCE:
+      return kt_naive_reduce_sum_f32((const float*)a->in0, a->d0, (double*)a->out0, (float*)a->out1, a->workspace,
+                                     a->ws_bytes, s);
+    case KT_OP_NAIVE_GEMM:
+      return kt_naive_gemm_f32((const float*)a->in0, (const float*)a->in1, (float*)a->out0, a->d0, a->d1, a->d2,
+                               a->i0, s);
+    case KT_OP_NAIVE_ATTENTION:
+      return kt_naive_attention_bf16((const uint16_t*)a->in0, (const uint16_t*)a->in1, (const uint16_t*)a->in2,
+                                     (uint16_t*)a->out0, a->d0, a->d1, a->d2, a->d3, a->f0, a->i0, s);
+    default:
+      return kt::fail(KT_ERR_ARG, "kt_run: unknown op %d", op);
+  }
+}
+
+int kt_time(int op, const kt_args* args, int warmup, int iters, void* flush, size_t flush_bytes, float* samples_ms,
+            kt_stream_t stream) {
+  kt::clear_error();
+  if (args == nullptr || warmup < 0 || iters < 0 || (iters > 0 && samples_ms == nullptr))
+    return kt::fail(KT_ERR_ARG, "kt_time: bad arguments");
+  for (int w = 0; w < warmup; ++w) {
+    int rc = kt_run(op, args, stream);
+    if (rc != KT_OK) return rc;
+  }
+  std::vector<cudaEvent_t> ev(2 * (size_t)iters, nullptr);
+  int rc = KT_OK;
+  for (size_t i = 0; i < ev.size() && rc == KT_OK; ++i) rc = kt::cuda_status(cudaEventCreate(&ev[i]), "kt_time: event");
+  for (int i = 0; i < iters && rc == KT_OK; ++i) {
+    rc = kt::flush_l2(flush, flush_bytes, stream);
+    if (rc == KT_OK) rc = kt::cuda_status(cudaEventRecord(ev[2 * i], stream), "kt_time: record");
+    if (rc == KT_OK) rc = kt_run(op, args, stream);
+    if (rc == KT_OK) rc = kt::cuda_status(cudaEventRecord(ev[2 * i + 1], stream), "kt_time: record");
+  }
+  if (rc == KT_OK) rc = kt::cuda_status(cudaStreamSynchronize(stream), "kt_time: synchronize");
+  for (int i = 0; i < iters && rc == KT_OK; ++i) {
+    float ms = 0.f;
+    rc = kt::cuda_status(cudaEventElapsedTime(&ms, ev[2 * i], ev[2 * i + 1]), "kt_time: elapsed");
+    samples_ms[i] = ms;
+  }
+  for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  return rc;
+}
+
+int kt_device_error(int reset, int* code_out) {
+  kt::clear_error();
+  int v = 0;
+  int rc = kt::cuda_status(cudaMemcpyFromSymbol(&v, g_kt_device_error, sizeof(int)), "kt_device_error: read");
+  if (rc != KT_OK) return rc;
+  if (code_out) *code_out = v;
+  if (reset) {
+    const int zero = 0;
+    rc = kt::cuda_status(cudaMemcpyToSymbol(g_kt_device_error, &zero, sizeof(int)), "kt_device_error: reset");
+  }
+  return rc;
+}
+
+}  // extern "C"

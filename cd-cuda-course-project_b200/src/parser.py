@@ -1,0 +1,258 @@
+"""
+parser.py — kernel profiles and the tuning search space.
+
+Keeps the reference's data model (src/parser.py:37-82: `MemoryAccessPattern`,
+`KernelInfo`, `KernelProfile`), its regex source scanner (src/parser.py:223-308)
+and `build_search_space(profile)` (src/parser.py:311-352), and adds the
+Blackwell axes the sm_100a kernels actually expose:
+
+  memory-bound rows (softmax, layernorm):
+      block_size, vec_per_thread (128-bit loads per thread, i.e. the row
+      capacity held in registers), min_blocks (occupancy hint)
+  reduction:
+      block_size, unroll (16-byte loads in flight per thread), blocks_per_sm
+  matmul:
+      variant {ffma, tf32}, transpose_b; ffma: bk (k tile);
+      tf32 (tcgen05): cta_tile (M×N of the TMEM accumulator), stages (TMA
+      pipeline depth), tma_box (k extent of one TMA box)
+  attention (tcgen05): kv_tile, stages
+
+Each axis is a template parameter of the kernel source (see generator.py),
+so every point of the space compiles to a distinct kernel. The reference's
+libclang parser is kept as an optional path (libclang is absent here and the
+regex scanner is used, as in the reference's fallback).
+"""
+
+from __future__ import annotations
+
+import re
+import warnings
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Optional
+
+try:
+    import clang.cindex as _ci  # noqa: F401
+    _LIBCLANG_OK = True
+except ImportError:
+    _ci = None  # type: ignore
+    _LIBCLANG_OK = False
+
+
+@dataclass
+class MemoryAccessPattern:
+    """Memory access characteristics extracted from kernel source."""
+    has_global_load: bool = False
+    has_global_store: bool = False
+    has_shared_mem: bool = False
+    has_coalesced_hint: bool = False
+    has_strided_access: bool = False
+    has_reduction: bool = False
+    has_warp_shuffle: bool = False
+    has_tma: bool = False
+    has_tensor_core: bool = False
+
+
+@dataclass
+class KernelInfo:
+    """Kernel metadata (superset of KernelProfile)."""
+    name: str
+    src_path: Path
+    param_names: list[str] = field(default_factory=list)
+    param_types: list[str] = field(default_factory=list)
+    param_count: int = 0
+    has_shared_mem: bool = False
+    has_unroll: bool = False
+    uses_threadidx: bool = False
+    uses_blockidx: bool = False
+    memory: MemoryAccessPattern = field(default_factory=MemoryAccessPattern)
+
+    def to_profile(self) -> "KernelProfile":
+        return KernelProfile(name=self.name, src_path=self.src_path, block_dim=0,
+                             uses_shared=self.has_shared_mem, loop_depth=1 if self.has_unroll else 0,
+                             memory=self.memory)
+
+
+@dataclass
+class KernelProfile:
+    """Optimisation-focused profile used by generator.py and search.py."""
+    name: str
+    src_path: Path
+    block_dim: int
+    uses_shared: bool
+    loop_depth: int
+    reduction_ops: list[str] = field(default_factory=list)
+    memory: MemoryAccessPattern = field(default_factory=MemoryAccessPattern)
+    raw_params: dict = field(default_factory=dict)
+
+
+# ---------------------------------------------------------------------------
+# Regex scanner (the reference's fallback parser, src/parser.py:223-308)
+# ---------------------------------------------------------------------------
+
+_RE_KERNEL = re.compile(r"__global__\s+(?:void\s+)?(?:__launch_bounds__\([^)]*\)\s*)?(?:void\s+)?(\w+)\s*\(")
+_RE_SHARED = re.compile(r"__shared__")
+_RE_STRIDE = re.compile(r"\[\s*\w+\s*\*\s*\w+\s*\+")
+_RE_REDUCTION = re.compile(r"\+=|block_sum|warp_sum|fmaxf")
+_RE_SHFL = re.compile(r"__shfl_\w+_sync")
+_RE_TMA = re.compile(r"cp\.async\.bulk")
+_RE_TC = re.compile(r"tcgen05\.mma")
+_RE_LOOP = re.compile(r"\bfor\s*\(")
+
+
+class RegexKernelParser:
+    """Find `__global__` kernels in a CUDA source and derive a KernelProfile each."""
+
+    def parse_to_profiles(self, src_path: Path) -> list[KernelProfile]:
+        src = Path(src_path).read_text(encoding="utf-8")
+        starts = [(m.group(1), m.start()) for m in _RE_KERNEL.finditer(src)]
+        out: list[KernelProfile] = []
+        for i, (name, start) in enumerate(starts):
+            end = starts[i + 1][1] if i + 1 < len(starts) else len(src)
+            body = src[start:end]
+            mem = MemoryAccessPattern(
+                has_global_load=True,
+                has_global_store=True,
+                has_shared_mem=bool(_RE_SHARED.search(body)),
+                has_strided_access=bool(_RE_STRIDE.search(body)),
+                has_reduction=bool(_RE_REDUCTION.search(body)),
+                has_warp_shuffle=bool(_RE_SHFL.search(body)) or "warp_sum" in body or "block_sum" in body,
+                has_tma=bool(_RE_TMA.search(body)),
+                has_tensor_core=bool(_RE_TC.search(body)),
+            )
+            out.append(KernelProfile(
+                name=name, src_path=Path(src_path), block_dim=0,
+                uses_shared=mem.has_shared_mem,
+                loop_depth=len(_RE_LOOP.findall(body)),
+                reduction_ops=_RE_REDUCTION.findall(body),
+                memory=mem,
+            ))
+        return out
+
+
+class LibclangKernelParser:  # pragma: no cover - libclang is not installed in this image
+    def __init__(self) -> None:
+        if not _LIBCLANG_OK:
+            raise RuntimeError("libclang (python package 'clang') is not installed")
+        raise RuntimeError("libclang parsing of sm_100a inline PTX is not supported; use RegexKernelParser")
+
+
+def make_parser():
+    """Return the best available parser (the regex scanner here)."""
+    if _LIBCLANG_OK:
+        try:
+            return LibclangKernelParser()
+        except Exception as e:  # noqa: BLE001
+            warnings.warn(f"libclang unavailable ({e}); using the regex parser.")
+    return RegexKernelParser()
+
+
+# ---------------------------------------------------------------------------
+# Family profiles and search spaces
+# ---------------------------------------------------------------------------
+
+FAMILIES = ("softmax", "layernorm", "reduction", "matmul", "attention")
+
+
+def family_of(profile_or_name) -> str:
+    name = profile_or_name.name if isinstance(profile_or_name, KernelProfile) else str(profile_or_name)
+    for fam in FAMILIES:
+        if name.startswith(fam):
+            return fam
+    raise ValueError(f"no kernel family for {name!r}")
+
+
+def build_kernel_profile(kernel: str, src_root: Optional[Path] = None) -> KernelProfile:
+    """Profile of a family's sm_100a source (the reference builds these by hand, autotune.py:98-115)."""
+    csrc = src_root or Path(__file__).resolve().parent.parent / "csrc"
+    src = {"softmax": "softmax.cuh", "layernorm": "layernorm.cuh", "reduction": "reduce.cuh",
+           "matmul": "gemm_tf32.cuh", "attention": "fa_fwd.cuh"}[kernel]
+    mem = MemoryAccessPattern(
+        has_global_load=True,
+        has_global_store=True,
+        has_strided_access=kernel == "matmul",
+        has_reduction=kernel in ("reduction", "softmax", "layernorm"),
+        has_shared_mem=kernel in ("matmul", "attention"),
+        has_warp_shuffle=kernel in ("reduction", "softmax", "layernorm"),
+        has_tma=kernel in ("matmul", "attention"),
+        has_tensor_core=kernel in ("matmul", "attention"),
+    )
+    return KernelProfile(name=kernel, src_path=csrc / src, block_dim=0, uses_shared=mem.has_shared_mem,
+                         loop_depth=2 if kernel == "matmul" else 1,
+                         reduction_ops=["+="] if mem.has_reduction else [], memory=mem)
+
+
+def build_search_space(profile: KernelProfile) -> dict:
+    """
+    Candidate parameter grid for a profile.
+
+    For the five sm_100a families the axes are the template parameters of
+    their kernels (module docstring). For any other profile the reference's
+    generic grid is returned (block_size × unroll × tile_x/tile_y ×
+    transpose_b × warp_shuffle, src/parser.py:311-352).
+    """
+    try:
+        fam = family_of(profile)
+    except ValueError:
+        fam = None
+    space: dict[str, list] = {}
+    if fam in ("softmax", "layernorm"):
+        space["block_size"] = [128, 256, 512, 1024]
+        space["vec_per_thread"] = [1, 2, 4, 8]
+        space["min_blocks"] = [1, 2, 4]
+    elif fam == "reduction":
+        space["block_size"] = [256, 512, 1024]
+        space["unroll"] = [2, 4, 8]
+        space["blocks_per_sm"] = [1, 2, 4, 8]
+    elif fam == "matmul":
+        space["variant"] = ["tf32", "ffma"]
+        space["transpose_b"] = [False, True]
+        space["bk"] = [8, 16, 32]
+        space["cta_tile"] = ["128x128", "128x256"]
+        space["stages"] = [3, 4, 5, 6]
+    elif fam == "attention":
+        space["kv_tile"] = [64, 128]
+        space["stages"] = [2, 3]
+        space["causal"] = [False, True]
+    else:
+        space["block_size"] = [64, 128, 192, 256]
+        space["unroll"] = [1, 2, 4, 8] if profile.loop_depth >= 1 else [1]
+        if not profile.uses_shared:
+            space["tile_x"] = [16, 32]
+            space["tile_y"] = [16, 32]
+        else:
+            space["tile_x"] = [16]
+            space["tile_y"] = [16]
+        space["transpose_b"] = [False, True] if profile.memory.has_strided_access else [False]
+        space["warp_shuffle"] = [False, True] if profile.memory.has_reduction else [False]
+    total = 1
+    for v in space.values():
+        total *= len(v)
+    space["_total_variants"] = total
+    space["_kernel"] = profile.name
+    return space
+
+
+def is_valid(kernel: str, params: dict) -> bool:
+    """Validity pruning (the reference prunes matmul tiles, src/generator.py:446-452)."""
+    if "tile_x" in params and "tile_y" in params:
+        # the reference's generic grid: square tiles no larger than the block
+        return params["tile_x"] == params["tile_y"] and params["tile_x"] <= params.get("block_size", 1 << 30)
+    fam = family_of(kernel) if kernel in FAMILIES else kernel
+    if fam in ("softmax", "layernorm"):
+        return params.get("block_size", 256) * params.get("min_blocks", 1) <= 2048
+    if fam == "reduction":
+        return params.get("block_size", 512) * params.get("blocks_per_sm", 1) <= 2048
+    if fam == "matmul":
+        if params.get("variant") == "ffma":
+            # the FFMA kernel ignores the tcgen05 axes: keep one representative point
+            return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
+        return params.get("bk", 16) == 16
+    return True
+
+
+if __name__ == "__main__":
+    for fam in FAMILIES:
+        prof = build_kernel_profile(fam)
+        sp = build_search_space(prof)
+        print(fam, sp["_total_variants"], {k: v for k, v in sp.items() if not k.startswith("_")})
