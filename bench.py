@@ -232,6 +232,7 @@ def main() -> None:
     import torch.distributed as dist
 
     import kt_lib
+    import sharding
     import workloads
     from roofline import RooflineAnalyzer, PEAKS
 
@@ -256,7 +257,7 @@ def main() -> None:
     ra = RooflineAnalyzer()
 
     def shard(n: int) -> tuple[int, int]:
-        return rank * n // world, (rank + 1) * n // world
+        return sharding.shard_range(n, world, rank)
 
     def pinned(a: np.ndarray) -> torch.Tensor:
         return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
@@ -284,8 +285,7 @@ def main() -> None:
             lib.reduce_sum_f32(src.data_ptr(), hi - lo, out64.data_ptr(), None, ws.data_ptr(), ws_bytes, sh)
 
         def collective():
-            if world > 1:
-                dist.all_reduce(out64)
+            sharding.combine_partials(out64)
 
         def e2e_in():
             x_e.copy_(x_h, non_blocking=True)
