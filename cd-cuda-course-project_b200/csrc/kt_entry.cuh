@@ -275,3 +275,6 @@ int kt_device_error(int reset, int* code_out) {
 }
 
 }  // extern "C"
+
+// Scratch-free variant of the reduction (fixed device-resident scratch).
+#include "reduce_noalloc.cu"

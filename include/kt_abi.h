@@ -119,6 +119,21 @@ size_t kt_reduce_workspace_bytes(int64_t n);
 int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
                       void* workspace, size_t ws_bytes, kt_stream_t stream);
 
+/* Same result as kt_reduce_sum_f32, for callers that cannot allocate device
+ * memory (host callbacks and real-time loops where cudaMalloc would block or
+ * synchronize, embedders with a fixed memory budget, FFI callers holding only
+ * their input/output buffers). It allocates nothing: the scratch is a fixed
+ * 16 KiB array (KT_NOALLOC_SCRATCH_BYTES; enough for grids of up to 2046 CTAs)
+ * in the library's own device memory, present on every device that uses the
+ * library until the process exits; a launch needing more returns
+ * KT_ERR_UNSUPPORTED. The first call on a device looks the array up with
+ * cudaGetSymbolAddress, so make that first call outside any stream capture.
+ * All calls on a device share the array: calls that may overlap on the GPU
+ * (unordered streams) race; order them on one stream.
+ * No counterpart in the reference (its executables allocate their own buffers). */
+#define KT_NOALLOC_SCRATCH_BYTES 16384
+int kt_reduce_sum_f32_noalloc(const float* x, int64_t n, double* out64, float* out32, kt_stream_t stream);
+
 /* C = A·B (transpose_b=0, B is K×N) or C = A·Bt^T (transpose_b=1, B holds Bt, N×K),
  * fp32 row-major, fp32 output. variant = KT_GEMM_FFMA | KT_GEMM_TF32.
  * Replaces `matmul_opt(const float* A, const float* B, float* C, int N)` with its
