@@ -36,7 +36,10 @@ BASE_FLAGS = [
     "-Xptxas", "-v",
     "--shared",
     "-Xcompiler", "-fPIC",
-    "-Xcompiler", "-fvisibility=default",
+    # hidden by default: only the KT_API entry points are exported, so the
+    # C++ internals of two loaded variants (including function-local statics,
+    # which GCC would otherwise make process-unique) never bind to each other
+    "-Xcompiler", "-fvisibility=hidden",
 ]
 
 

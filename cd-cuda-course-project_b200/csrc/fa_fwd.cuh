@@ -6,7 +6,7 @@ namespace kt {
 namespace fa {
 
 inline int launch(const uint16_t*, const uint16_t*, const uint16_t*, uint16_t*, int64_t, int64_t, int64_t, int64_t,
-                  float, int, int*, cudaStream_t) {
+                  float, int, cudaStream_t) {
   return fail(KT_ERR_UNSUPPORTED, "flash-attention forward: not implemented yet");
 }
 

@@ -166,7 +166,10 @@ inline int launch(const float* A, const float* B, float* C, int64_t M, int64_t N
                   cudaStream_t st) {
   if (M < 0 || N < 0 || K < 0) return fail(KT_ERR_ARG, "gemm: negative shape");
   if (M == 0 || N == 0) return KT_OK;
-  if (!A || !B || !C) return fail(KT_ERR_ARG, "gemm: null pointer");
+  if (!C) return fail(KT_ERR_ARG, "gemm: null C");
+  // with K == 0 nothing of A or B is read and C = 0
+  if (K == 0) return cuda_status(cudaMemsetAsync(C, 0, sizeof(float) * (size_t)M * (size_t)N, st), "gemm: zero C");
+  if (!A || !B) return fail(KT_ERR_ARG, "gemm: null pointer");
   if ((M + BM - 1) / BM > 65535) return fail(KT_ERR_UNSUPPORTED, "gemm: M too large for the grid");
   const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && (K % 4 == 0) && (tb ? true : (N % 4 == 0)) &&
                    (N % 4 == 0);

@@ -64,15 +64,17 @@ enum DeviceErr : int {
   DEV_BAD_SHAPE = 2       // a kernel-side bounds check refused an index
 };
 
-// Defined once in kt_runtime.cu (relocatable device code is not used, so each
-// translation unit that needs it receives the address as a kernel argument).
-struct DevErr {
-  int* word;
-};
+}  // namespace kt
 
-__device__ __forceinline__ void raise_device_error(int* word, int code) {
-  if (word != nullptr) atomicCAS(word, 0, code);
-}
+// Device error word of this library (one translation unit per library, so one
+// word per library and device). Kernels name it directly; host code reads it
+// with cudaMemcpyFromSymbol (kt_device_error).
+static __device__ int g_kt_device_error = 0;
+
+namespace kt {
+
+// First error wins; later ones are dropped.
+__device__ __forceinline__ void raise_device_error(int code) { atomicCAS(&g_kt_device_error, 0, code); }
 
 // Streaming 128-bit read that does not allocate in L1 (data read once).
 __device__ __forceinline__ float4 ld_stream4(const float4* p) {

@@ -59,9 +59,6 @@
 #define KT_VARIANT_JSON "{\"variant\": \"default\"}"
 #endif
 
-// Device error word shared by every kernel of this library that has bounded waits.
-__device__ int g_kt_device_error = 0;
-
 namespace kt {
 
 static thread_local char g_last_error[512] = {0};
@@ -150,7 +147,7 @@ int kt_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
   kt::clear_error();
 #if KT_WITH_GEMM
   if (variant == KT_GEMM_FFMA) return kt::gemm_ffma::launch(A, B, C, M, N, K, transpose_b, stream);
-  if (variant == KT_GEMM_TF32) return kt::gemm_tf32::launch(A, B, C, M, N, K, transpose_b, &g_kt_device_error, stream);
+  if (variant == KT_GEMM_TF32) return kt::gemm_tf32::launch(A, B, C, M, N, K, transpose_b, stream);
   return kt::fail(KT_ERR_ARG, "gemm: unknown variant %d", variant);
 #else
   return kt::unsupported("gemm");
@@ -161,7 +158,7 @@ int kt_fa_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint
                    int64_t S, int64_t D, float scale, int causal, kt_stream_t stream) {
   kt::clear_error();
 #if KT_WITH_FA
-  return kt::fa::launch(Q, K, V, O, B, H, S, D, scale, causal, &g_kt_device_error, stream);
+  return kt::fa::launch(Q, K, V, O, B, H, S, D, scale, causal, stream);
 #else
   return kt::unsupported("flash-attention forward");
 #endif

@@ -185,19 +185,28 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // UMMA shared-memory descriptor (64 bit):
 //   [0,14)  start address >> 4        [16,30) leading-dimension byte offset >> 4
 //   [32,46) stride-dimension byte offset >> 4
-//   [46,48) version = 1 (sm_100)     [49,52) base offset (0: atoms 1024-byte aligned)
-//   [52]    LBO mode = 0              [61,64) layout: 2 = 128-byte swizzle
-// K-major SW128: rows of 128 bytes, 8-row groups SBO = 1024 bytes apart, LBO unused (1).
-// MN-major SW128: 128-byte MN chunks; LBO = byte distance between consecutive
-// MN chunks, SBO = byte distance between 8-row K groups.
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+//   [46,48) version = 1 (sm_100)     [49,52) base offset (0: atoms aligned)
+//   [52]    LBO mode = 0              [61,64) layout type
+// Layout 2 (128-byte swizzle, 16-byte chunks XOR row%8):
+//   K-major: rows of 128 bytes, 8-row groups SBO = 1024 bytes apart, LBO unused (16).
+// Layout 1 (128-byte swizzle with 32-byte chunks XOR row%4) — the only
+// MN-major layout for 32-bit (tf32) operands:
+//   128-byte MN chunks (32 elements) per K row; LBO = byte distance between
+//   consecutive MN chunks, SBO = byte distance between 4-row K groups (512).
+constexpr uint32_t kLayoutSW128 = 2, kLayoutSW128Base32B = 1;
+
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return make_desc(saddr, lbo_bytes, sbo_bytes, kLayoutSW128);
 }
 
 // Instruction descriptor for kind::tf32 / kind::f16 with fp32 accumulation:
@@ -233,9 +242,12 @@ inline PFN_encodeTiled get_encode_tiled() {
 }
 
 // Row-major 2-D tensor (rows × cols, leading dim `ld` elements) with a box of
-// box_cols × box_rows elements and 128-byte swizzle; out-of-bounds reads fill zero.
+// box_cols × box_rows elements (box_cols × elem_bytes <= 128) and a 128-byte
+// swizzle (16-byte chunks by default, 32-byte chunks with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B); out-of-bounds reads fill zero.
 inline int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, const void* base,
-                        uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows) {
+                        uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
+                        CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   PFN_encodeTiled enc = get_encode_tiled();
   if (enc == nullptr) return fail(KT_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint64_t dims[2] = {cols, rows};
@@ -243,7 +255,7 @@ inline int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return KT_OK;
 }

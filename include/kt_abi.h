@@ -34,6 +34,13 @@ extern "C" {
 
 typedef struct CUstream_st* kt_stream_t; /* identical to cudaStream_t */
 
+/* Libraries are built with hidden visibility; only these entry points are exported. */
+#if defined(__GNUC__)
+#define KT_API __attribute__((visibility("default")))
+#else
+#define KT_API
+#endif
+
 /* Status codes. The reference mapped every failure (CUDA_CHECK → exit(1),
  * non-zero return, timeout) to `None` in Python (src/benchmark.py:135-152). */
 enum {
@@ -86,29 +93,29 @@ typedef struct kt_args {
 } kt_args;
 
 /* Thread-local text of the last error raised on the calling thread ("" if none). */
-const char* kt_last_error(void);
+KT_API const char* kt_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-int kt_version(void);
+KT_API int kt_version(void);
 
 /* JSON object with the template parameters baked into this build
  * (the reference recorded them only in the generated file's header comment,
  * src/generator.py:29-33). */
-const char* kt_variant_params(void);
+KT_API const char* kt_variant_params(void);
 
 /* Row softmax y[r,:] = exp(x[r,:]-max)/sum, fp32 in/out, rows×cols row-major.
  * Replaces `softmax_opt(const float* in, float* out, int rows, int cols)`
  * (src/generator.py:110-153) and `softmax_naive` (src/kernels/baseline_kernels.cu:52-77). */
-int kt_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kt_stream_t stream);
+KT_API int kt_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kt_stream_t stream);
 
 /* LayerNorm over the last dim: y = gamma*(x-mean)/sqrt(var+eps)+beta, biased var.
  * Replaces `layernorm_opt(in, out, gamma, beta, rows, cols, eps)`
  * (src/generator.py:166-213) and `layernorm_naive` (src/kernels/baseline_kernels.cu:110-142). */
-int kt_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y,
+KT_API int kt_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y,
                      int64_t rows, int64_t cols, float eps, kt_stream_t stream);
 
 /* Bytes of device scratch kt_reduce_sum_f32 needs for n elements. */
-size_t kt_reduce_workspace_bytes(int64_t n);
+KT_API size_t kt_reduce_workspace_bytes(int64_t n);
 
 /* Full sum of n fp32 values, accumulated in fp64; writes *out64 (device) and,
  * when out32 != NULL, the fp32-rounded sum to *out32 (device). `workspace`
@@ -116,7 +123,7 @@ size_t kt_reduce_workspace_bytes(int64_t n);
  * Replaces `reduction_opt(const float* in, float* out, int N)`, which only
  * produced per-block partials (src/generator.py:82-98, :302-324), and
  * `reduction_naive` (src/kernels/baseline_kernels.cu:83-104). */
-int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
+KT_API int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
                       void* workspace, size_t ws_bytes, kt_stream_t stream);
 
 /* Same result as kt_reduce_sum_f32, for callers that cannot allocate device
@@ -132,14 +139,14 @@ int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
  * (unordered streams) race; order them on one stream.
  * No counterpart in the reference (its executables allocate their own buffers). */
 #define KT_NOALLOC_SCRATCH_BYTES 16384
-int kt_reduce_sum_f32_noalloc(const float* x, int64_t n, double* out64, float* out32, kt_stream_t stream);
+KT_API int kt_reduce_sum_f32_noalloc(const float* x, int64_t n, double* out64, float* out32, kt_stream_t stream);
 
 /* C = A·B (transpose_b=0, B is K×N) or C = A·Bt^T (transpose_b=1, B holds Bt, N×K),
  * fp32 row-major, fp32 output. variant = KT_GEMM_FFMA | KT_GEMM_TF32.
  * Replaces `matmul_opt(const float* A, const float* B, float* C, int N)` with its
  * `transpose_b` load (src/generator.py:40-70, :286-299) and `matmul_naive`
  * (src/kernels/baseline_kernels.cu:32-46). */
-int kt_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+KT_API int kt_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                 int transpose_b, int variant, kt_stream_t stream);
 
 /* Flash-attention forward, bf16 Q/K/V/O laid out [B,H,S,D] contiguous, fp32
@@ -147,26 +154,26 @@ int kt_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, 
  * Replaces `attention_flash` / `attention_tiled(Q,K,V,O,S,D)` (single head, fp32;
  * src/attention.py:210-291, :75-176) and `attention_naive`
  * (src/kernels/baseline_kernels.cu:149-181). */
-int kt_fa_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
+KT_API int kt_fa_fwd_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
                    int64_t B, int64_t H, int64_t S, int64_t D, float scale, int causal,
                    kt_stream_t stream);
 
 /* Naive GPU baselines (one thread per row / per output element) used as the
  * Welch-t reference point, restating the algorithms of
  * src/kernels/baseline_kernels.cu:32-181 (timed by src/kernels/benchmark_runner.cu:236-359). */
-int kt_naive_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kt_stream_t stream);
-int kt_naive_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y,
+KT_API int kt_naive_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, kt_stream_t stream);
+KT_API int kt_naive_layernorm_f32(const float* x, const float* gamma, const float* beta, float* y,
                            int64_t rows, int64_t cols, float eps, kt_stream_t stream);
-int kt_naive_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
+KT_API int kt_naive_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
                             void* workspace, size_t ws_bytes, kt_stream_t stream);
-int kt_naive_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+KT_API int kt_naive_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
                       int transpose_b, kt_stream_t stream);
-int kt_naive_attention_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
+KT_API int kt_naive_attention_bf16(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O,
                             int64_t B, int64_t H, int64_t S, int64_t D, float scale, int causal,
                             kt_stream_t stream);
 
 /* Dispatch one op by id (see kt_args). */
-int kt_run(int op, const kt_args* args, kt_stream_t stream);
+KT_API int kt_run(int op, const kt_args* args, kt_stream_t stream);
 
 /* In-process timing: `warmup` untimed runs, then `iters` samples, each
  * bracketed by its own CUDA event pair on `stream`; between samples the
@@ -175,12 +182,12 @@ int kt_run(int op, const kt_args* args, kt_stream_t stream);
  * samples_ms (host memory) and synchronizes the stream before returning.
  * Replaces the per-variant `main()` timing loop (src/generator.py:255-271) and
  * `time_kernel` (src/kernels/benchmark_runner.cu:74-104). */
-int kt_time(int op, const kt_args* args, int warmup, int iters, void* flush, size_t flush_bytes,
+KT_API int kt_time(int op, const kt_args* args, int warmup, int iters, void* flush, size_t flush_bytes,
             float* samples_ms, kt_stream_t stream);
 
 /* Device error word written by kernels whose bounded waits gave up
  * (0 = none). Reading it synchronizes the device. reset != 0 clears it. */
-int kt_device_error(int reset, int* code_out);
+KT_API int kt_device_error(int reset, int* code_out);
 
 #ifdef __cplusplus
 }
