@@ -1,0 +1,123 @@
+"""
+GPU parity of flash-attention forward (bf16 Q/K/V/O, [B, H, S, D]) through the
+C ABI against the fp64 oracle evaluated on the same bf16 inputs.
+
+Tolerance: normwise max|O-ref|/max|ref| <= 2e-2 (BASELINE budget for bf16
+attention; the bf16 output rounding alone is ~4e-3). On the reference's
+known-answer inputs (S=512, D=64, Q=sin, K=cos, V=sin; src/verifier.py:181-191)
+the result is also compared with the reference's own fp32 output.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+import kt_lib  # noqa: E402
+import kt_ops  # noqa: E402
+import workloads  # noqa: E402
+from oracle import ref  # noqa: E402
+
+TOL = 2e-2
+
+
+def to_dev_bf16(bits: np.ndarray, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(dev).view(torch.bfloat16)
+
+
+def run(lib, dev, q, k, v, scale, causal):
+    o = kt_ops.fa_fwd(to_dev_bf16(q, dev), to_dev_bf16(k, dev), to_dev_bf16(v, dev), scale=scale, causal=causal,
+                      lib=lib)
+    torch.cuda.synchronize()
+    return workloads.bf16_to_f32(o.view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+def oracle(q, k, v, scale, causal):
+    return ref.attention_ref(workloads.bf16_to_f32(q), workloads.bf16_to_f32(k), workloads.bf16_to_f32(v),
+                             scale, causal)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_reference_kat(dev, lib, golden, causal):
+    Q, K, V = ref.kat_attention_inputs(512, 64)
+    q, k, v = (workloads.bf16_bits(a.reshape(1, 1, 512, 64)) for a in (Q, K, V))
+    o = run(lib, dev, q, k, v, 1.0 / 8.0, causal)
+    assert ref.normwise_rel_err(o, oracle(q, k, v, 1.0 / 8.0, causal)) <= TOL
+    if not causal:
+        # against the reference's own fp32 result: its inputs are not bf16, and
+        # the outputs are small averages (|O| <= 0.022), so rounding the inputs
+        # to bf16 already moves the exact result by ~1.6e-2 normwise; the
+        # kernel may add at most its own budget on top of that
+        quant = ref.normwise_rel_err(oracle(q, k, v, 1.0 / 8.0, False).ravel(), golden["attention_S512_D64"])
+        assert ref.normwise_rel_err(o.ravel(), golden["attention_S512_D64"]) <= quant + TOL
+
+
+SHAPES = [(1, 1, 128, 128), (2, 3, 256, 128), (1, 2, 1000, 128), (2, 2, 384, 64), (1, 1, 77, 64), (1, 1, 4096, 128)]
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("B,H,S,D", SHAPES)
+def test_attention_shapes(dev, lib, B, H, S, D, causal):
+    inp = workloads.make_inputs("attention", d={"B": B, "H": H, "S": S, "D": D}, seed=B * 1000 + H * 100 + S + D)
+    o = run(lib, dev, inp["q"], inp["k"], inp["v"], inp["scale"], causal)
+    want = oracle(inp["q"], inp["k"], inp["v"], inp["scale"], causal)
+    assert ref.normwise_rel_err(o, want) <= TOL
+    assert lib.device_error() == 0
+
+
+def test_attention_large_scores_rescale(dev, lib):
+    # a growing score scale forces the running max to rise by > 2^8 several times
+    B, H, S, D = 1, 2, 1024, 128
+    rng = np.random.default_rng(8)
+    q = rng.standard_normal((B, H, S, D), dtype=np.float32) * 3.0
+    k = rng.standard_normal((B, H, S, D), dtype=np.float32) * np.linspace(0.2, 3.0, S, dtype=np.float32)[:, None]
+    v = rng.standard_normal((B, H, S, D), dtype=np.float32)
+    qb, kb, vb = (workloads.bf16_bits(a) for a in (q, k, v))
+    for causal in (False, True):
+        o = run(lib, dev, qb, kb, vb, 1.0 / math.sqrt(D), causal)
+        assert ref.normwise_rel_err(o, oracle(qb, kb, vb, 1.0 / math.sqrt(D), causal)) <= TOL
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_config_size_sampled_heads(dev, lib, causal):
+    inp = workloads.make_inputs("attention", "config")
+    q, k, v = (to_dev_bf16(inp[n], dev) for n in ("q", "k", "v"))
+    o1 = kt_ops.fa_fwd(q, k, v, scale=inp["scale"], causal=causal, lib=lib)
+    o2 = kt_ops.fa_fwd(q, k, v, scale=inp["scale"], causal=causal, lib=lib)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)  # deterministic
+    got = o1.view(torch.int16).cpu().numpy().view(np.uint16)
+    for b, h in ((0, 0), (3, 17), (7, 31)):
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        want = oracle(inp["q"][sl], inp["k"][sl], inp["v"][sl], inp["scale"], causal)
+        assert ref.normwise_rel_err(workloads.bf16_to_f32(got[sl]), want) <= TOL
+    assert lib.device_error() == 0
+
+
+def test_attention_errors(dev, lib):
+    with pytest.raises(kt_lib.KtError) as ei:
+        lib.fa_fwd_bf16(0, 0, 0, 0, 1, 1, 128, 128, 0.1, False)
+    assert ei.value.status == kt_lib.KT_ERR_ARG
+    x = torch.zeros((1, 1, 128, 96), dtype=torch.bfloat16, device=dev)
+    with pytest.raises(kt_lib.KtError) as ei:
+        kt_ops.fa_fwd(x, x, x, lib=lib)
+    assert ei.value.status == kt_lib.KT_ERR_UNSUPPORTED
+
+
+def test_naive_attention_matches(dev, lib):
+    inp = workloads.make_inputs("attention", d={"B": 1, "H": 2, "S": 200, "D": 64}, seed=3)
+    q, k, v = (to_dev_bf16(inp[n], dev) for n in ("q", "k", "v"))
+    o = torch.empty_like(q)
+    for causal in (False, True):
+        lib.run("naive_attention", kt_lib.make_args(in0=q.data_ptr(), in1=k.data_ptr(), in2=v.data_ptr(),
+                                                    out0=o.data_ptr(), d0=1, d1=2, d2=200, d3=64,
+                                                    f0=inp["scale"], i0=int(causal)))
+        torch.cuda.synchronize()
+        got = workloads.bf16_to_f32(o.view(torch.int16).cpu().numpy().view(np.uint16))
+        assert ref.normwise_rel_err(got, oracle(inp["q"], inp["k"], inp["v"], inp["scale"], causal)) <= TOL
