@@ -12,6 +12,7 @@
 // The reference template reads x three times (src/generator.py:182-212).
 #pragma once
 #include "kt_common.cuh"
+#include "rows_staged.cuh"
 
 #ifndef KT_LN_BLOCK
 #define KT_LN_BLOCK 256
@@ -21,6 +22,9 @@
 #endif
 #ifndef KT_LN_MINB
 #define KT_LN_MINB 1
+#endif
+#ifndef KT_LN_STAGES
+#define KT_LN_STAGES 3  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
 #endif
 
 namespace kt {
@@ -209,6 +213,16 @@ inline int launch(const float* x, const float* gamma, const float* beta, float* 
   const unsigned g = (unsigned)(rows < max_grid ? rows : max_grid);
   if (c <= CAP) {
     if ((c & 3) == 0 && aligned16(x) && aligned16(y) && aligned16(gamma) && aligned16(beta)) {
+      if (KT_LN_STAGES > 0 && staged::smem_bytes<(KT_LN_STAGES > 0 ? KT_LN_STAGES : 1)>(c) <= 200 * 1024) {
+        constexpr int ST = KT_LN_STAGES > 0 ? KT_LN_STAGES : 1;
+        auto kern = staged::layernorm_rows<BLOCK, VPT, ST>;
+        const size_t smem = staged::smem_bytes<ST>(c);
+        int grid = 0;
+        int rc = staged::launch_grid(kern, BLOCK, smem, rows, &grid);
+        if (rc != KT_OK) return rc;
+        kern<<<grid, BLOCK, smem, st>>>(x, gamma, beta, y, rows, c, eps);
+        return check_launch("layernorm staged rows");
+      }
       rows_vec<BLOCK, VPT, KT_LN_MINB><<<g, BLOCK, 0, st>>>(x, gamma, beta, y, rows, c, eps);
       return check_launch("layernorm rows_vec");
     }

@@ -95,6 +95,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 1-D bulk copy global -> CTA shared memory (TMA engine, no tensor map);
+// both addresses 16-byte aligned, bytes a multiple of 16; completion as
+// transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 // TMEM allocation is warp-wide (.sync.aligned); the base address is written to
 // shared memory at `dst`. ncols: power of two in [32, 512].

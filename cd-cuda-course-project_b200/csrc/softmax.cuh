@@ -18,6 +18,7 @@
 // reciprocal of the row sum.
 #pragma once
 #include "kt_common.cuh"
+#include "rows_staged.cuh"
 
 #ifndef KT_SOFTMAX_BLOCK
 #define KT_SOFTMAX_BLOCK 256
@@ -27,6 +28,9 @@
 #endif
 #ifndef KT_SOFTMAX_MINB
 #define KT_SOFTMAX_MINB 1
+#endif
+#ifndef KT_SOFTMAX_STAGES
+#define KT_SOFTMAX_STAGES 3  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
 #endif
 
 namespace kt {
@@ -208,6 +212,16 @@ inline int launch(const float* x, float* y, int64_t rows, int64_t cols, cudaStre
   const unsigned g = (unsigned)(rows < max_grid ? rows : max_grid);
   if (c <= CAP) {
     if ((c & 3) == 0 && aligned16(x) && aligned16(y)) {
+      if (KT_SOFTMAX_STAGES > 0 && staged::smem_bytes<(KT_SOFTMAX_STAGES > 0 ? KT_SOFTMAX_STAGES : 1)>(c) <= 200 * 1024) {
+        constexpr int ST = KT_SOFTMAX_STAGES > 0 ? KT_SOFTMAX_STAGES : 1;
+        auto kern = staged::softmax_rows<BLOCK, VPT, ST>;
+        const size_t smem = staged::smem_bytes<ST>(c);
+        int grid = 0;
+        int rc = staged::launch_grid(kern, BLOCK, smem, rows, &grid);
+        if (rc != KT_OK) return rc;
+        kern<<<grid, BLOCK, smem, st>>>(x, y, rows, c);
+        return check_launch("softmax staged rows");
+      }
       rows_vec<BLOCK, VPT, KT_SOFTMAX_MINB><<<g, BLOCK, 0, st>>>(x, y, rows, c);
       return check_launch("softmax rows_vec");
     }

@@ -51,11 +51,13 @@ def variants_dir() -> Path:
 
 # parameter -> macro, per family; parameters absent here are runtime arguments
 MACROS: dict[str, dict[str, str]] = {
-    "softmax": {"block_size": "KT_SOFTMAX_BLOCK", "vec_per_thread": "KT_SOFTMAX_VPT", "min_blocks": "KT_SOFTMAX_MINB"},
-    "layernorm": {"block_size": "KT_LN_BLOCK", "vec_per_thread": "KT_LN_VPT", "min_blocks": "KT_LN_MINB"},
+    "softmax": {"block_size": "KT_SOFTMAX_BLOCK", "vec_per_thread": "KT_SOFTMAX_VPT", "min_blocks": "KT_SOFTMAX_MINB",
+                "stages": "KT_SOFTMAX_STAGES"},
+    "layernorm": {"block_size": "KT_LN_BLOCK", "vec_per_thread": "KT_LN_VPT", "min_blocks": "KT_LN_MINB",
+                  "stages": "KT_LN_STAGES"},
     "reduction": {"block_size": "KT_REDUCE_BLOCK", "unroll": "KT_REDUCE_UNROLL", "blocks_per_sm": "KT_REDUCE_BPSM"},
     "matmul": {"bk": "KT_FFMA_BK", "cta_tile": "KT_TC_BN", "stages": "KT_TC_STAGES"},
-    "attention": {"kv_tile": "KT_FA_BN", "stages": "KT_FA_STAGES"},
+    "attention": {"kv_tile": "KT_FA_BN", "stages": "KT_FA_STAGES", "poly_exp2": "KT_FA_POLY"},
 }
 ONLY = {"softmax": "KT_ONLY_SOFTMAX", "layernorm": "KT_ONLY_LAYERNORM", "reduction": "KT_ONLY_REDUCE",
         "matmul": "KT_ONLY_GEMM", "attention": "KT_ONLY_FA"}

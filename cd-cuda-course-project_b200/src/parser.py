@@ -8,14 +8,15 @@ Blackwell axes the sm_100a kernels actually expose:
 
   memory-bound rows (softmax, layernorm):
       block_size, vec_per_thread (128-bit loads per thread, i.e. the row
-      capacity held in registers), min_blocks (occupancy hint)
+      capacity held in registers), min_blocks (occupancy hint), stages
+      (rows in flight per CTA through a TMA bulk-copy ring; 0 = register kernel)
   reduction:
       block_size, unroll (16-byte loads in flight per thread), blocks_per_sm
   matmul:
       variant {ffma, tf32}, transpose_b; ffma: bk (k tile);
       tf32 (tcgen05): cta_tile (M×N of the TMEM accumulator), stages (TMA
       pipeline depth), tma_box (k extent of one TMA box)
-  attention (tcgen05): kv_tile, stages
+  attention (tcgen05): stages (K/V ring depth), poly_exp2 (FMA-pipe exponentials)
 
 Each axis is a template parameter of the kernel source (see generator.py),
 so every point of the space compiles to a distinct kernel. The reference's
@@ -200,6 +201,7 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["block_size"] = [128, 256, 512, 1024]
         space["vec_per_thread"] = [1, 2, 4, 8]
         space["min_blocks"] = [1, 2, 4]
+        space["stages"] = [0, 2, 3, 4]    # 0: one row per CTA in registers; n: TMA bulk-copy ring of n rows
     elif fam == "reduction":
         space["block_size"] = [256, 512, 1024]
         space["unroll"] = [2, 4, 8]
@@ -211,8 +213,8 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["cta_tile"] = ["128x128", "128x256"]
         space["stages"] = [3, 4, 5, 6]
     elif fam == "attention":
-        space["kv_tile"] = [64, 128]
-        space["stages"] = [2, 3]
+        space["stages"] = [2, 3]          # K/V ring depth
+        space["poly_exp2"] = [0, 1]       # share of exponentials on the FMA pipe
         space["causal"] = [False, True]
     else:
         space["block_size"] = [64, 128, 192, 256]
@@ -240,6 +242,8 @@ def is_valid(kernel: str, params: dict) -> bool:
         return params["tile_x"] == params["tile_y"] and params["tile_x"] <= params.get("block_size", 1 << 30)
     fam = family_of(kernel) if kernel in FAMILIES else kernel
     if fam in ("softmax", "layernorm"):
+        if params.get("stages", 0) > 0 and params.get("min_blocks", 1) != 1:
+            return False  # the staged kernel sizes its grid by occupancy; min_blocks only shapes the register kernel
         return params.get("block_size", 256) * params.get("min_blocks", 1) <= 2048
     if fam == "reduction":
         return params.get("block_size", 512) * params.get("blocks_per_sm", 1) <= 2048

@@ -275,3 +275,24 @@ def test_kt_time_samples(dev, lib):
     assert len(samples) == 10 and all(0.0 < s < 50.0 for s in samples)
     softmax_ok(y.cpu().numpy(), x)
     assert lib.device_error() == 0
+
+
+@pytest.mark.parametrize("fam", ["softmax", "layernorm"])
+def test_register_kernel_variant(dev, lib, tmp_path, monkeypatch, fam):
+    """The one-row-per-CTA register kernels (stages=0), built as a tuning variant;
+    the default library runs the TMA bulk-copy ring for these shapes."""
+    monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
+    import generator
+    ok, log, so = generator.ensure_variant(fam, {"block_size": 256, "vec_per_thread": 4, "min_blocks": 1,
+                                                 "stages": 0})
+    assert ok, log
+    v = kt_lib.KtLibrary(so)
+    for rows, cols in ((257, 4096), (33, 1028), (4096, 4096)):
+        inp = workloads.make_inputs(fam, d={"rows": rows, "cols": cols}, seed=rows + cols)
+        if fam == "softmax":
+            y = kt_ops.softmax(to_dev(inp["x"], dev), lib=v).cpu().numpy()
+            softmax_ok(y, inp["x"])
+        else:
+            y = kt_ops.layernorm(to_dev(inp["x"], dev), to_dev(inp["gamma"], dev), to_dev(inp["beta"], dev),
+                                 inp["eps"], lib=v).cpu().numpy()
+            layernorm_ok(y, inp["x"], inp["gamma"], inp["beta"], inp["eps"])

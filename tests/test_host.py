@@ -68,9 +68,9 @@ def _space():
 
 
 def _objective(p):
-    # smooth synthetic latency, minimum at block 256, vec 4, min_blocks 2
+    # smooth synthetic latency, minimum at block 256, vec 4, min_blocks 1, stages 3
     return (1.0 + (math.log2(p["block_size"]) - 8) ** 2 + (math.log2(p["vec_per_thread"]) - 2) ** 2
-            + 0.5 * (math.log2(p["min_blocks"]) - 1) ** 2)
+            + 0.5 * math.log2(p["min_blocks"]) ** 2 + 0.25 * (p["stages"] - 3) ** 2)
 
 
 def test_grid_strategy_covers_valid_points():
@@ -81,12 +81,12 @@ def test_grid_strategy_covers_valid_points():
     assert all(kparser.is_valid("softmax", p) for p in pts)
     for p in pts:
         g.update(p, _objective(p))
-    assert g.best() == {"block_size": 256, "vec_per_thread": 4, "min_blocks": 2}
+    assert g.best() == {"block_size": 256, "vec_per_thread": 4, "min_blocks": 1, "stages": 3}
 
 
 def test_bayesian_strategy_finds_optimum_within_budget():
     sp = _space()
-    bo = search.BayesianOptStrategy(sp, "softmax", n_calls=20, seed=3)
+    bo = search.BayesianOptStrategy(sp, "softmax", n_calls=30, seed=3)
     n = 0
     while True:
         batch = bo.suggest(1)
@@ -95,8 +95,8 @@ def test_bayesian_strategy_finds_optimum_within_budget():
         for p in batch:
             bo.update(p, _objective(p))
             n += 1
-    assert n == 20
-    assert _objective(bo.best()) <= 1.5  # at or next to the optimum after 20 of 48 points
+    assert n == 30
+    assert _objective(bo.best()) <= 1.5  # at or next to the optimum after 30 of the grid's points
 
 
 def test_bayesian_strategy_handles_failures():
