@@ -16,7 +16,8 @@ Blackwell axes the sm_100a kernels actually expose:
       variant {ffma, tf32}, transpose_b; ffma: bk (k tile);
       tf32 (tcgen05): cta_tile (M×N of the TMEM accumulator), stages (TMA
       pipeline depth), tma_box (k extent of one TMA box)
-  attention (tcgen05): stages (K/V ring depth), poly_exp2 (FMA-pipe exponentials)
+  attention (tcgen05): stages (K ring depth), v_stages (V ring depth),
+      poly_exp2 (FMA-pipe exponentials)
 
 Each axis is a template parameter of the kernel source (see generator.py),
 so every point of the space compiles to a distinct kernel. The reference's
@@ -213,7 +214,8 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["cta_tile"] = ["128x128", "128x256"]
         space["stages"] = [3, 4, 5, 6]
     elif fam == "attention":
-        space["stages"] = [2, 3]          # K/V ring depth
+        space["stages"] = [2, 3, 4]       # K ring depth
+        space["v_stages"] = [2, 3]        # V ring depth
         space["poly_exp2"] = [0, 1]       # share of exponentials on the FMA pipe
         space["causal"] = [False, True]
     else:
@@ -252,6 +254,9 @@ def is_valid(kernel: str, params: dict) -> bool:
             # the FFMA kernel ignores the tcgen05 axes: keep one representative point
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
         return params.get("bk", 16) == 16
+    if fam == "attention":
+        # head dim 128: Q + (K + V slots) x 32 KB must fit the 227 KB of shared memory
+        return params.get("stages", 3) + params.get("v_stages", 2) <= 5
     return True
 
 
