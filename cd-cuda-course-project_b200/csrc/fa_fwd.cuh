@@ -23,8 +23,8 @@
 //              rows of lane quarter w%4 and split their 128 score columns in
 //              halves. Per tile: the half-row maxima are exchanged through shared
 //              memory (one mbarrier per warp pair, bounded wait), p =
-//              2^(s·scale·log2e − m) for the own half (every 4th pair of values
-//              by a polynomial on the FMA pipe, the rest by MUFU ex2), bf16 P back
+//              2^(s·scale·log2e − m) for the own half (MUFU ex2; optionally every
+//              4th pair by a polynomial on the FMA pipe), bf16 P back
 //              to TMEM, partial row sum. The running max is only raised (O and
 //              the sums rescaled) when it grows by more than 2^8, so O is rarely
 //              touched. Final O / l in bf16.
@@ -45,7 +45,8 @@
 #define KT_FA_BN 128
 #endif
 #ifndef KT_FA_POLY
-#define KT_FA_POLY 1  // share of exponentials on the FMA pipe: every 4th value pair when 1
+#define KT_FA_POLY 0  // 1: every 4th value pair of exponentials on the FMA pipe (measured slower: the FMA/ALU
+                      // pipes, not MUFU, limit the softmax warps)
 #endif
 
 namespace kt {
@@ -55,7 +56,8 @@ constexpr int BM = 128;
 constexpr int BN = 128;  // keys per tile (the S accumulator is 128 columns)
 constexpr int SOFTMAX_WARPS = 8;
 constexpr int V_LOADER_WARP = 2 + SOFTMAX_WARPS;
-constexpr int THREADS = 96 + 32 * SOFTMAX_WARPS;
+constexpr int EPI_THREADS = 128;  // warps 11-14: one query row per thread
+constexpr int THREADS = 96 + 32 * SOFTMAX_WARPS + EPI_THREADS;
 constexpr int SOFTMAX_THREADS = 32 * SOFTMAX_WARPS;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only when the max grows by > 2^8
 constexpr int kHeadGroup = 8;              // causal scheduling: heads whose K/V share L2
@@ -68,15 +70,15 @@ struct Cfg {
   static constexpr int Q_BYTES = REGIONS * SLAB;    // 128 rows × D bf16
   static constexpr int K_BYTES = REGIONS * SLAB;    // BN keys × D
   static constexpr int V_BYTES = REGIONS * SLAB;
-  static constexpr int Q_OFFSET = 0;
-  static constexpr int K_OFFSET = Q_BYTES;
+  static constexpr int Q_OFFSET = 0;                // two Q buffers: the next item's tile loads early
+  static constexpr int K_OFFSET = 2 * Q_BYTES;
   static constexpr int V_OFFSET = K_OFFSET + STAGES * K_BYTES;
-  // softmax exchange: [2 parity][2 half][128 rows] maxima + [2 half][128 rows] row sums
+  // [2 tile parity][2 half][128 rows] softmax maxima + [2 item parity][2 half][128 rows] row sums
   static constexpr int RED_OFFSET = V_OFFSET + VSTAGES * V_BYTES;
-  static constexpr int BAR_OFFSET = RED_OFFSET + 6 * 128 * 4;
-  // q_full, k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[2], s_free[2], p_full[2],
-  // o_done, o_final, done, pair[4]
-  static constexpr int NUM_BARS = 1 + 2 * STAGES + 2 * VSTAGES + 2 + 2 + 2 + 1 + 1 + 1 + 4;
+  static constexpr int BAR_OFFSET = RED_OFFSET + 8 * 128 * 4;
+  // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[2], s_free[2],
+  // p_full[2], l_full[2], l_empty[2], o_done, o_final, o_empty, done, pair[4]
+  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 10 + 4 + 4;
   static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
@@ -113,60 +115,82 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
+// Work item w (one 128-row query tile of one (b, h)) -> (qt, bh). Items are
+// taken in index order by the persistent CTAs (item = CTA, CTA + grid, ...),
+// so the items in flight together are adjacent. Non-causal: the query tiles
+// of one head are adjacent (its K/V stays in L2). Causal: heads in groups of
+// kHeadGroup, inside a group the heaviest (latest) query tiles first.
+template <bool CAUSAL>
+__device__ __forceinline__ void item_coords(int w, int num_q_tiles, int BH, int& qt, int& bh) {
+  if (CAUSAL) {
+    const int per_group = kHeadGroup * num_q_tiles;
+    const int group = w / per_group;
+    const int r = w - group * per_group;
+    const int gsize = min(kHeadGroup, BH - group * kHeadGroup);
+    qt = num_q_tiles - 1 - r / gsize;
+    bh = group * kHeadGroup + r % gsize;
+  } else {
+    qt = w % num_q_tiles;
+    bh = w / num_q_tiles;
+  }
+}
+
+template <bool CAUSAL>
+__device__ __forceinline__ int kv_tiles(int qt, int S) {
+  const int all = (S + BN - 1) / BN;
+  return CAUSAL ? min(all, (qt * BM + BM - 1) / BN + 1) : all;
+}
+
 template <int D, int STAGES, bool CAUSAL>
 __global__ void __launch_bounds__(THREADS, 1)
 fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-              const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ O, int S, float scale_log2) {
+              const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ O, int S, int BH,
+              float scale_log2) {
   using CF = Cfg<D, STAGES>;
   using namespace sm100;
+  constexpr int VSTAGES = KT_FA_VSTAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw);
   float* red = reinterpret_cast<float*>(base_ptr + CF::RED_OFFSET);
   const uint32_t bar0 = base + CF::BAR_OFFSET;
-  constexpr int VSTAGES = KT_FA_VSTAGES;
-  constexpr int R = 1 + 2 * STAGES + 2 * VSTAGES;  // first barrier after the load rings
-  const uint32_t q_full = bar0;
-  auto k_full = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto k_empty = [&](int s) { return bar0 + 8u * (1 + STAGES + s); };
-  auto v_full = [&](int s) { return bar0 + 8u * (1 + 2 * STAGES + s); };
-  auto v_empty = [&](int s) { return bar0 + 8u * (1 + 2 * STAGES + VSTAGES + s); };
+  // barrier map (8 bytes each)
+  auto q_full = [&](int s) { return bar0 + 8u * s; };
+  auto q_empty = [&](int s) { return bar0 + 8u * (2 + s); };
+  auto k_full = [&](int s) { return bar0 + 8u * (4 + s); };
+  auto k_empty = [&](int s) { return bar0 + 8u * (4 + STAGES + s); };
+  auto v_full = [&](int s) { return bar0 + 8u * (4 + 2 * STAGES + s); };
+  auto v_empty = [&](int s) { return bar0 + 8u * (4 + 2 * STAGES + VSTAGES + s); };
+  constexpr int R = 4 + 2 * STAGES + 2 * VSTAGES;
   auto s_full = [&](int b) { return bar0 + 8u * (R + b); };
   auto s_free = [&](int b) { return bar0 + 8u * (R + 2 + b); };
   auto p_full = [&](int b) { return bar0 + 8u * (R + 4 + b); };
-  const uint32_t o_done = bar0 + 8u * (R + 6);     // one phase per P·V product
-  const uint32_t o_final = bar0 + 8u * (R + 7);    // single use: the last P·V product landed
-  const uint32_t done_bar = bar0 + 8u * (R + 8);
-  const uint32_t pair_bar0 = bar0 + 8u * (R + 9);  // 4 softmax warp-pair exchanges
+  auto l_full = [&](int b) { return bar0 + 8u * (R + 6 + b); };
+  auto l_empty = [&](int b) { return bar0 + 8u * (R + 8 + b); };
+  const uint32_t o_done = bar0 + 8u * (R + 10);   // one phase per P·V product
+  const uint32_t o_final = bar0 + 8u * (R + 11);  // one phase per item: its last P·V product landed
+  const uint32_t o_empty = bar0 + 8u * (R + 12);  // one phase per item: the epilogue has read O
+  const uint32_t done_bar = bar0 + 8u * (R + 13);
+  const uint32_t pair_bar0 = bar0 + 8u * (R + 14);  // 4 softmax warp-pair exchanges
   const uint32_t tmem_slot = bar0 + 8u * CF::NUM_BARS;
   const volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<const volatile uint32_t*>(base_ptr + CF::BAR_OFFSET + 8 * CF::NUM_BARS);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_q_tiles = (S + BM - 1) / BM;
-  // 1-D grid, blocks start in index order. Non-causal: the query tiles of one
-  // head are adjacent, so the CTAs running together share that head's K/V in
-  // L2. Causal: heads in groups of kHeadGroup (K/V of a group stays in L2),
-  // inside a group the heaviest (latest) query tiles first.
-  int qt, bh;
-  if (CAUSAL) {
-    const int per_group = kHeadGroup * num_q_tiles;
-    const int group = (int)blockIdx.x / per_group;
-    const int r = (int)blockIdx.x - group * per_group;
-    const int gsize = min(kHeadGroup, (int)(gridDim.x / num_q_tiles) - group * kHeadGroup);
-    qt = num_q_tiles - 1 - r / gsize;
-    bh = group * kHeadGroup + r % gsize;
-  } else {
-    qt = (int)blockIdx.x % num_q_tiles;
-    bh = (int)blockIdx.x / num_q_tiles;
-  }
-  const int q0 = qt * BM;
-  const int num_kv_all = (S + BN - 1) / BN;
-  const int n_kv = CAUSAL ? min(num_kv_all, (q0 + BM - 1) / BN + 1) : num_kv_all;
+  const int num_items = BH * num_q_tiles;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(q_full(s), 1);
+      mbar_init(q_empty(s), 1);
+      mbar_init(s_full(s), 1);
+      mbar_init(s_free(s), SOFTMAX_THREADS);
+      mbar_init(p_full(s), SOFTMAX_THREADS);
+      mbar_init(l_full(s), SOFTMAX_THREADS);
+      mbar_init(l_empty(s), EPI_THREADS);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
@@ -175,13 +199,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full(b), 1);
-      mbar_init(s_free(b), SOFTMAX_THREADS);
-      mbar_init(p_full(b), SOFTMAX_THREADS);
-    }
     mbar_init(o_done, 1);
     mbar_init(o_final, 1);
+    mbar_init(o_empty, EPI_THREADS);
     mbar_init(done_bar, 1);
     for (int q = 0; q < 4; ++q) mbar_init(pair_bar0 + 8u * q, 64);
     fence_mbar_init();
@@ -201,42 +221,62 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 
   if (warp == 0 || warp == V_LOADER_WARP) {
     if (lane == 0) {
-      // warp 0: Q once, then K tiles; warp V_LOADER_WARP: V tiles
+      // warp 0: Q of every item (2 buffers) and the K tiles; V_LOADER_WARP: the V tiles.
+      // Ring positions run on across items.
       const bool is_k = (warp == 0);
+      constexpr int MAXS = STAGES > VSTAGES ? STAGES : VSTAGES;
       const int nst = is_k ? STAGES : VSTAGES;
-      if (is_k) {
-        const uint32_t q_dst = base + CF::Q_OFFSET;
-        mbar_arrive_expect_tx(q_full, CF::Q_BYTES);
+      uint32_t last_ph[MAXS];
+      bool pending[MAXS];
+      bool q_pending[2] = {false, false};
+      uint32_t q_last_ph[2] = {0u, 0u};
 #pragma unroll
-        for (int r = 0; r < CF::REGIONS; ++r) tma_load_3d(q_dst + r * CF::SLAB, &tm_q, 64 * r, q0, bh, q_full);
-      }
+      for (int i = 0; i < MAXS; ++i) pending[i] = false;
       int s = 0;
       uint32_t ph = 0;
-      uint32_t last_ph[STAGES > VSTAGES ? STAGES : VSTAGES];
-      bool pending[STAGES > VSTAGES ? STAGES : VSTAGES];
+      int k = 0;
+      for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
+        int qt, bh;
+        item_coords<CAUSAL>(w, num_q_tiles, BH, qt, bh);
+        const int n_kv = kv_tiles<CAUSAL>(qt, S);
+        if (is_k) {
+          const int qb = k & 1;
+          const uint32_t qph = (uint32_t)(k >> 1) & 1u;
+          if (!mbar_wait(q_empty(qb), qph ^ 1u)) {
+            timed_out = true;
+            break;
+          }
+          mbar_arrive_expect_tx(q_full(qb), CF::Q_BYTES);
 #pragma unroll
-      for (int i = 0; i < (STAGES > VSTAGES ? STAGES : VSTAGES); ++i) pending[i] = false;
-      for (int j = 0; j < n_kv; ++j) {
-        const uint32_t empty = is_k ? k_empty(s) : v_empty(s);
-        const uint32_t full = is_k ? k_full(s) : v_full(s);
-        if (!mbar_wait(empty, ph ^ 1u)) {
-          timed_out = true;
-          break;
+          for (int r = 0; r < CF::REGIONS; ++r)
+            tma_load_3d(base + CF::Q_OFFSET + qb * CF::Q_BYTES + r * CF::SLAB, &tm_q, 64 * r, qt * BM, bh, q_full(qb));
+          q_pending[qb] = true;
+          q_last_ph[qb] = qph;
         }
-        const uint32_t dst = base + (is_k ? CF::K_OFFSET + s * CF::K_BYTES : CF::V_OFFSET + s * CF::V_BYTES);
-        mbar_arrive_expect_tx(full, CF::K_BYTES);
+        for (int j = 0; j < n_kv; ++j) {
+          const uint32_t empty = is_k ? k_empty(s) : v_empty(s);
+          const uint32_t full = is_k ? k_full(s) : v_full(s);
+          if (!mbar_wait(empty, ph ^ 1u)) {
+            timed_out = true;
+            break;
+          }
+          const uint32_t dst = base + (is_k ? CF::K_OFFSET + s * CF::K_BYTES : CF::V_OFFSET + s * CF::V_BYTES);
+          mbar_arrive_expect_tx(full, CF::K_BYTES);
 #pragma unroll
-        for (int r = 0; r < CF::REGIONS; ++r)
-          tma_load_3d(dst + r * CF::SLAB, is_k ? &tm_k : &tm_v, 64 * r, j * BN, bh, full);
-        last_ph[s] = ph;
-        pending[s] = true;
-        if (++s == nst) {
-          s = 0;
-          ph ^= 1u;
+          for (int r = 0; r < CF::REGIONS; ++r)
+            tma_load_3d(dst + r * CF::SLAB, is_k ? &tm_k : &tm_v, 64 * r, j * BN, bh, full);
+          last_ph[s] = ph;
+          pending[s] = true;
+          if (++s == nst) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
       }
       if (timed_out) {
-        if (is_k) (void)mbar_wait(q_full, 0);
+        // let every copy still in flight land before the CTA exits
+        for (int i = 0; i < 2; ++i)
+          if (q_pending[i]) (void)mbar_wait(q_full(i), q_last_ph[i]);
         for (int i = 0; i < nst; ++i)
           if (pending[i]) (void)mbar_wait(is_k ? k_full(i) : v_full(i), last_ph[i]);
       }
@@ -245,205 +285,248 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f32acc(kFmtBF16, BM, BN, 0, 0);
       constexpr uint32_t idesc_o = idesc_f32acc(kFmtBF16, BM, D, 0, 1);
-      const uint32_t q_src = base + CF::Q_OFFSET;
-      auto issue_s = [&](int j, int stage) {
-        const uint32_t k_src = base + CF::K_OFFSET + stage * CF::K_BYTES;
-        const uint32_t d_tmem = tmem + CF::COL_S + (uint32_t)((j & 1) * BN);
+      int kc = 0, vc = 0;  // K / V ring positions
+      // descriptors as (lo, hi) words: lo + byte offset / 16 addresses base + offset
+      const uint64_t dk = desc_sw128(base, 16u, 1024u);                  // K-major operands (Q, K)
+      const uint64_t dv = desc_sw128(base, (uint32_t)CF::SLAB, 1024u);   // V, MN-major
+      const uint32_t k_hi = (uint32_t)(dk >> 32), v_hi = (uint32_t)(dv >> 32);
+      const uint32_t q_lo0 = (uint32_t)dk + (CF::Q_OFFSET >> 4);
+      const uint32_t k_lo0 = (uint32_t)dk + (CF::K_OFFSET >> 4);
+      const uint32_t v_lo0 = (uint32_t)dv + (CF::V_OFFSET >> 4);
+      // S_t = Q·K^T into S buffer t&1 from K slot kc
+      auto issue_s = [&](int t, int qb) {
+        const uint32_t q_lo = q_lo0 + (uint32_t)qb * (CF::Q_BYTES >> 4);
+        const uint32_t k_lo = k_lo0 + (uint32_t)(kc % STAGES) * (CF::K_BYTES >> 4);
+        const uint32_t d_tmem = tmem + CF::COL_S + (uint32_t)((t & 1) * BN);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * CF::SLAB + (kk & 3) * 32);
-          mma_f16_ss(d_tmem, desc_sw128(q_src + off, 16u, 1024u), desc_sw128(k_src + off, 16u, 1024u), idesc_s,
-                     kk > 0 ? 1u : 0u);
+          const uint32_t off = (uint32_t)(((kk >> 2) * CF::SLAB + (kk & 3) * 32) >> 4);
+          mma_f16_ss_w(d_tmem, q_lo + off, k_hi, k_lo + off, k_hi, idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(s_full(j & 1));
-        mma_commit(k_empty(stage));  // the K slot is free once S_j has read it
+        mma_commit(s_full(t & 1));
+        mma_commit(k_empty(kc % STAGES));  // the K slot is free once S_t has read it
+        ++kc;
       };
-      auto issue_pv = [&](int j, int stage) {
-        const uint32_t v_src = base + CF::V_OFFSET + stage * CF::V_BYTES;
-        const uint32_t p_tmem = tmem + CF::COL_P + (uint32_t)((j & 1) * 64);
+      // O += P_t·V (O = P_t·V for the first tile of an item); needs P_t and the V tile
+      auto pv_step = [&](int t, int k, bool first, bool last) -> bool {
+        if (!mbar_wait(p_full(t & 1), (uint32_t)(t >> 1) & 1u)) return false;
+        if (!mbar_wait(v_full(vc % VSTAGES), (uint32_t)(vc / VSTAGES) & 1u)) return false;
+        // the epilogue must have read the previous item's O before it is overwritten
+        if (first && !mbar_wait(o_empty, ((uint32_t)k & 1u) ^ 1u)) return false;
+        tc_fence_after();
+        const uint32_t v_lo = v_lo0 + (uint32_t)(vc % VSTAGES) * (CF::V_BYTES >> 4);
+        const uint32_t p_tmem = tmem + CF::COL_P + (uint32_t)((t & 1) * 64);
+        const uint32_t o_tmem = tmem + CF::COL_O;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // 16 keys per MMA: rows 16kk..16kk+15 of every 64-column V slab; slabs CF::SLAB apart
-          const uint64_t vd = desc_sw128(v_src + (uint32_t)(kk * 16 * 128), (uint32_t)CF::SLAB, 1024u);
-          mma_f16_ts(tmem + CF::COL_O, p_tmem + (uint32_t)(kk * 8), vd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts_w(o_tmem, p_tmem + (uint32_t)(kk * 8), v_lo + (uint32_t)(kk * 16 * 128 / 16), v_hi, idesc_o,
+                       (!first || kk > 0) ? 1u : 0u);
         }
         mma_commit(o_done);
-        mma_commit(v_empty(stage));
-      };
-      // P·V of tile j: needs P_j from the softmax and V_j from its ring
-      auto pv_step = [&](int j) -> bool {
-        if (!mbar_wait(p_full(j & 1), (uint32_t)(j >> 1) & 1u)) return false;
-        if (!mbar_wait(v_full(j % VSTAGES), (uint32_t)(j / VSTAGES) & 1u)) return false;
-        tc_fence_after();
-        issue_pv(j, j % VSTAGES);
+        mma_commit(v_empty(vc % VSTAGES));
+        if (last) mma_commit(o_final);
+        ++vc;
         return true;
       };
-      if (!mbar_wait(q_full, 0)) timed_out = true;
-      tc_fence_after();
-      for (int j = 0; j < n_kv && !timed_out; ++j) {
-        if (!mbar_wait(k_full(j % STAGES), (uint32_t)(j / STAGES) & 1u)) {
+      // Issue order S_t, P_{t-1}·V: the tensor core computes the next scores while
+      // the softmax warps work on the current ones, across item boundaries too.
+      int t = 0, k = 0;
+      bool have_prev = false, prev_first = false, prev_last = false;
+      int prev_k = 0;
+      for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
+        int qt, bh;
+        item_coords<CAUSAL>(w, num_q_tiles, BH, qt, bh);
+        const int n_kv = kv_tiles<CAUSAL>(qt, S);
+        if (!mbar_wait(q_full(k & 1), (uint32_t)(k >> 1) & 1u)) {
           timed_out = true;
           break;
         }
-        // S buffer j&1 was last read by the softmax of tile j-2
-        if (!mbar_wait(s_free(j & 1), ((uint32_t)(j >> 1) & 1u) ^ 1u)) {
-          timed_out = true;
-          break;
-        }
-        tc_fence_after();
-        issue_s(j, j % STAGES);
-        if (j > 0 && !pv_step(j - 1)) {
-          timed_out = true;
-          break;
+        for (int j = 0; j < n_kv; ++j, ++t) {
+          // K tile, and S buffer t&1 last read by the softmax of tile t-2
+          if (!mbar_wait(k_full(kc % STAGES), (uint32_t)(kc / STAGES) & 1u) ||
+              !mbar_wait(s_free(t & 1), ((uint32_t)(t >> 1) & 1u) ^ 1u)) {
+            timed_out = true;
+            break;
+          }
+          tc_fence_after();
+          issue_s(t, k & 1);
+          if (j == n_kv - 1) mma_commit(q_empty(k & 1));
+          if (have_prev && !pv_step(t - 1, prev_k, prev_first, prev_last)) {
+            timed_out = true;
+            break;
+          }
+          have_prev = true;
+          prev_first = (j == 0);
+          prev_last = (j == n_kv - 1);
+          prev_k = k;
         }
       }
-      if (!timed_out && n_kv > 0) {
-        if (pv_step(n_kv - 1)) mma_commit(o_final);
-        else timed_out = true;
-      }
+      if (!timed_out && have_prev && !pv_step(t - 1, prev_k, prev_first, prev_last)) timed_out = true;
       mma_commit(done_bar);
     }
-  } else {
+  } else if (warp < V_LOADER_WARP) {
     // softmax: TMEM lane quarter = warp % 4, the two warps of a quarter split the columns
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
-    const int qrow = q0 + row;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t pair_mbar = pair_bar0 + 8u * (uint32_t)quarter;  // mbarrier of the two warps of this quarter
-    uint32_t pair_uses = 0;                                        // completed exchanges (phase count)
-    constexpr int HC = BN / 2;                         // score columns per thread
-    constexpr int HD = D / 2;                          // O columns per thread
-    float m_run = -INFINITY;  // running max of s·scale·log2e used by the exponentials (same in both halves)
-    float l_part = 0.f;       // this half's share of the row sum
-    for (int j = 0; j < n_kv; ++j) {
-      const int b = j & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full(b), (uint32_t)(j >> 1) & 1u))) {
-        timed_out = true;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(b * BN + half * HC);
-      const int key0 = j * BN + half * HC;
-      const bool mask_tile = (CAUSAL && j * BN + BN - 1 > q0) || (j * BN + BN > S);
-      uint32_t sv[HC];
-#pragma unroll
-      for (int c = 0; c < HC; c += 32) tmem_ld32(s_addr + (uint32_t)c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
-      tmem_ld_wait();
-      if (mask_tile) {
-#pragma unroll
-        for (int t = 0; t < HC; ++t) {
-          const int key = key0 + t;
-          if (!(key < S && (!CAUSAL || key <= qrow))) sv[t] = __float_as_uint(-INFINITY);
-        }
-      }
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int t = 0; t < HC; ++t) m4[t & 3] = fmaxf(m4[t & 3], __uint_as_float(sv[t]));
-      // exchange the half-row maxima (parity-double-buffered: the partner may
-      // still read the previous tile's slot while this thread writes the next)
-      float* red_max = red + (b * 2) * 128;
-      red_max[half * 128 + row] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      mbar_arrive(pair_mbar);  // release: the write above is visible to the partner after its wait
-      if (!__all_sync(0xffffffffu, mbar_wait(pair_mbar, pair_uses & 1u))) {
-        timed_out = true;
-        break;
-      }
-      ++pair_uses;
-      const float mx = fmaxf(red_max[row], red_max[128 + row]);
-      const float m_tile = mx * scale_log2;
-      const bool raise = m_tile > m_run + kRescaleThreshold;
-      float alpha = 1.f;
-      if (raise) {
-        alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_tile);
-        m_run = m_tile;
-        l_part *= alpha;
-      }
-      // O holds P_0..P_{j-1}·V: rescale this half of it once the previous PV
-      // product has landed. o_done is at phase j-1 or j here (s_full[j] was
-      // committed after PV_{j-2} was issued, and PV_j needs this thread's P_j),
-      // so a parity wait is exact.
-      if (j > 0 && __any_sync(0xffffffffu, raise)) {
-        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (uint32_t)(j - 1) & 1u))) {
+    constexpr int HC = BN / 2;                                     // score columns per thread
+    constexpr int HD = D / 2;                                      // O columns per thread (rescale)
+    int t = 0, k = 0;
+    for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
+      int qt, bh;
+      item_coords<CAUSAL>(w, num_q_tiles, BH, qt, bh);
+      const int n_kv = kv_tiles<CAUSAL>(qt, S);
+      const int q0 = qt * BM;
+      const int qrow = q0 + row;
+      float m_run = -INFINITY;  // running max of s·scale·log2e used by the exponentials (same in both halves)
+      float l_part = 0.f;       // this half's share of the row sum
+      for (int j = 0; j < n_kv; ++j, ++t) {
+        const int b = t & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full(b), (uint32_t)(t >> 1) & 1u))) {
           timed_out = true;
           break;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          uint32_t v[32];
-          const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)(half * HD + c);
-          tmem_ld32(oa, v);
-          tmem_ld_wait();
-          uint32_t w0[16], w1[16];
+        const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(b * BN + half * HC);
+        const int key0 = j * BN + half * HC;
+        const bool mask_tile = (CAUSAL && j * BN + BN - 1 > q0) || (j * BN + BN > S);
+        uint32_t sv[HC];
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            w0[t] = __float_as_uint(__uint_as_float(v[t]) * alpha);
-            w1[t] = __float_as_uint(__uint_as_float(v[16 + t]) * alpha);
+        for (int c = 0; c < HC; c += 32) tmem_ld32(s_addr + (uint32_t)c, *reinterpret_cast<uint32_t(*)[32]>(&sv[c]));
+        tmem_ld_wait();
+        if (mask_tile) {
+#pragma unroll
+          for (int c = 0; c < HC; ++c) {
+            const int key = key0 + c;
+            if (!(key < S && (!CAUSAL || key <= qrow))) sv[c] = __float_as_uint(-INFINITY);
           }
-          tmem_st16(oa, w0);
-          tmem_st16(oa + 16u, w1);
         }
-        tmem_st_wait();
-      }
-      // p = 2^(s·c − m) (masked entries are −inf -> 0), partial sum, bf16 P into TMEM
-      const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2));
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < HC; c += 32) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const float x0 = fmaf(__uint_as_float(sv[c + 2 * t]), scale_log2, -m_run);
-          const float x1 = fmaf(__uint_as_float(sv[c + 2 * t + 1]), scale_log2, -m_run);
-          float p0, p1;
-          if (KT_FA_POLY && !mask_tile && (t & 3) == 3) {
-            p0 = ex2_poly(x0);
-            p1 = ex2_poly(x1);
-          } else {
-            p0 = ex2(x0);
-            p1 = ex2(x1);
+        for (int c = 0; c < HC; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sv[c]));
+        // exchange the half-row maxima (slots double-buffered by tile parity: the
+        // partner may still read the previous tile's slot while this thread writes)
+        float* red_max = red + (b * 2) * 128;
+        red_max[half * 128 + row] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mbar_arrive(pair_mbar);  // release: the write above is visible to the partner after its wait
+        if (!__all_sync(0xffffffffu, mbar_wait(pair_mbar, (uint32_t)t & 1u))) {
+          timed_out = true;
+          break;
+        }
+        const float mx = fmaxf(red_max[row], red_max[128 + row]);
+        const float m_tile = mx * scale_log2;
+        const bool raise = m_tile > m_run + kRescaleThreshold;
+        float alpha = 1.f;
+        if (raise) {
+          alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_tile);
+          m_run = m_tile;
+          l_part *= alpha;
+        }
+        // O holds P_0..P_{j-1}·V of this item: rescale this half of it once the
+        // previous P·V product has landed. o_done has completed t-1 or t phases
+        // here (s_full of tile t was committed after P_{t-2}·V was issued, and
+        // P_t·V needs this thread's P_t), so a parity wait is exact.
+        if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(o_done, (uint32_t)(t - 1) & 1u))) {
+            timed_out = true;
+            break;
           }
-          s4[t & 3] += p0 + p1;
-          pk[t] = pack_bf16(p0, p1);
-        }
-        tmem_st16(p_addr + (uint32_t)(c / 2), pk);
-      }
-      l_part += (s4[0] + s4[1]) + (s4[2] + s4[3]);
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(s_free(b));
-      mbar_arrive(p_full(b));
-    }
-    // epilogue: O / l -> bf16 (each half writes its D/2 columns)
-    if (!timed_out && n_kv > 0) {
-      float* red_l = red + 4 * 128;  // own slot: no reader of the max slots can be overwritten
-      red_l[half * 128 + row] = l_part;
-      mbar_arrive(pair_mbar);
-      const bool pair_ok = __all_sync(0xffffffffu, mbar_wait(pair_mbar, pair_uses & 1u));
-      const float l_run = red_l[row] + red_l[128 + row];
-      if (!pair_ok || !__all_sync(0xffffffffu, mbar_wait(o_final, 0))) {
-        timed_out = true;
-      } else {
-        tc_fence_after();
-        const float inv = 1.0f / l_run;
-        __nv_bfloat16* orow = O + ((int64_t)bh * S + qrow) * D + half * HD;
+          tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          uint32_t v[32];
-          tmem_ld32(tmem + lane_off + CF::COL_O + (uint32_t)(half * HD + c), v);
-          tmem_ld_wait();
-          if (qrow < S) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t v[32];
+            const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)(half * HD + c);
+            tmem_ld32(oa, v);
+            tmem_ld_wait();
+            uint32_t w0[16], w1[16];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              uint4 w;
-              w.x = pack_bf16(__uint_as_float(v[8 * t + 0]) * inv, __uint_as_float(v[8 * t + 1]) * inv);
-              w.y = pack_bf16(__uint_as_float(v[8 * t + 2]) * inv, __uint_as_float(v[8 * t + 3]) * inv);
-              w.z = pack_bf16(__uint_as_float(v[8 * t + 4]) * inv, __uint_as_float(v[8 * t + 5]) * inv);
-              w.w = pack_bf16(__uint_as_float(v[8 * t + 6]) * inv, __uint_as_float(v[8 * t + 7]) * inv);
-              dst[t] = w;
+            for (int i = 0; i < 16; ++i) {
+              w0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              w1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
             }
+            tmem_st16(oa, w0);
+            tmem_st16(oa + 16u, w1);
+          }
+          tmem_st_wait();
+        }
+        // p = 2^(s·c − m) (masked entries are −inf -> 0), partial sum, bf16 P into TMEM
+        const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2));
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < HC; c += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float x0 = fmaf(__uint_as_float(sv[c + 2 * i]), scale_log2, -m_run);
+            const float x1 = fmaf(__uint_as_float(sv[c + 2 * i + 1]), scale_log2, -m_run);
+            float p0, p1;
+            if (KT_FA_POLY && !mask_tile && (i & 3) == 3) {
+              p0 = ex2_poly(x0);
+              p1 = ex2_poly(x1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            s4[i & 3] += p0 + p1;
+            pk[i] = pack_bf16(p0, p1);
+          }
+          tmem_st16(p_addr + (uint32_t)(c / 2), pk);
+        }
+        l_part += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(s_free(b));
+        mbar_arrive(p_full(b));
+      }
+      if (timed_out) break;
+      // hand this half's row sum to the epilogue warps (two slots, by item parity)
+      const int lb = k & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(l_empty(lb), ((uint32_t)(k >> 1) & 1u) ^ 1u))) {
+        timed_out = true;
+        break;
+      }
+      red[(4 + 2 * lb + half) * 128 + row] = l_part;
+      mbar_arrive(l_full(lb));
+    }
+  } else {
+    // epilogue warps: O / l -> bf16, one query row per thread; O is released to the
+    // next item's first P·V product as soon as it is in registers
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    int k = 0;
+    for (int w = blockIdx.x; w < num_items; w += gridDim.x, ++k) {
+      int qt, bh;
+      item_coords<CAUSAL>(w, num_q_tiles, BH, qt, bh);
+      const int qrow = qt * BM + row;
+      const int lb = k & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(o_final, (uint32_t)k & 1u)) ||
+          !__all_sync(0xffffffffu, mbar_wait(l_full(lb), (uint32_t)(k >> 1) & 1u))) {
+        timed_out = true;
+        break;
+      }
+      const float l_run = red[(4 + 2 * lb) * 128 + row] + red[(5 + 2 * lb) * 128 + row];
+      mbar_arrive(l_empty(lb));
+      tc_fence_after();
+      const float inv = 1.0f / l_run;
+      uint4* dst = reinterpret_cast<uint4*>(O + ((int64_t)bh * S + qrow) * D);
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + CF::COL_O + (uint32_t)c, v);
+        tmem_ld_wait();
+        if (c + 32 == D) {
+          tc_fence_before();
+          mbar_arrive(o_empty);  // all of O is in registers: the next item may overwrite it
+        }
+        if (qrow < S) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* f = reinterpret_cast<const float*>(v) + 8 * i;
+            dst[c / 8 + i] = make_uint4(pack_bf16(f[0] * inv, f[1] * inv), pack_bf16(f[2] * inv, f[3] * inv),
+                                        pack_bf16(f[4] * inv, f[5] * inv), pack_bf16(f[6] * inv, f[7] * inv));
           }
         }
       }
@@ -483,7 +566,7 @@ inline int launch_t(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uin
   if (rc == KT_OK) rc = make_tmap_bhsd(&tv, V, BH, S, D);
   if (rc != KT_OK) return rc;
   auto kern = fa_fwd_kernel<D, KT_FA_STAGES, CAUSAL>;
-  static bool attr_set = false;
+  static bool attr_set = false;  // one flag per template instance
   if (!attr_set) {
     rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES),
                      "attention: smem attribute");
@@ -491,9 +574,12 @@ inline int launch_t(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uin
     attr_set = true;
   }
   const float scale_log2 = scale * 1.4426950408889634f;  // log2(e)
-  const int64_t blocks = BH * ((S + BM - 1) / BM);
-  dim3 grid((unsigned)blocks);
-  kern<<<grid, THREADS, CF::SMEM_BYTES, st>>>(tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(O), (int)S, scale_log2);
+  // persistent: one CTA per SM (TMEM holds one CTA's 512 columns), items strided over the CTAs
+  const int64_t items = BH * ((S + BM - 1) / BM);
+  const int64_t sms = sm_count();
+  dim3 grid((unsigned)(items < sms ? items : sms));
+  kern<<<grid, THREADS, CF::SMEM_BYTES, st>>>(tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(O), (int)S, (int)BH,
+                                              scale_log2);
   return check_launch("attention fwd");
 }
 

@@ -214,8 +214,8 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["cta_tile"] = ["128x128", "128x256"]
         space["stages"] = [3, 4, 5, 6]
     elif fam == "attention":
-        space["stages"] = [2, 3, 4]       # K ring depth
-        space["v_stages"] = [2, 3]        # V ring depth
+        space["stages"] = [1, 2, 3]       # K ring depth
+        space["v_stages"] = [1, 2, 3]     # V ring depth
         space["poly_exp2"] = [0, 1]       # share of exponentials on the FMA pipe
         space["causal"] = [False, True]
     else:
@@ -255,8 +255,8 @@ def is_valid(kernel: str, params: dict) -> bool:
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
         return params.get("bk", 16) == 16
     if fam == "attention":
-        # head dim 128: Q + (K + V slots) x 32 KB must fit the 227 KB of shared memory
-        return params.get("stages", 3) + params.get("v_stages", 2) <= 5
+        # head dim 128: two Q buffers + (K + V slots) x 32 KB must fit the 227 KB of shared memory
+        return params.get("stages", 2) + params.get("v_stages", 2) <= 4
     return True
 
 
