@@ -59,14 +59,22 @@ from search import ConvergenceLogger, make_strategy  # noqa: E402
 SUPPORTED_KERNELS = list(FAMILIES)
 RECYCLE_AFTER = 48  # variant libraries loaded per worker before it is replaced
 
-# __global__ function (substring of the mangled name) and block size per family for occupancy
-KERNEL_FUNCTION = {
-    "softmax": ("rows_vec", lambda p: p.get("block_size", 256)),
-    "layernorm": ("rows_vec", lambda p: p.get("block_size", 256)),
-    "reduction": ("sum_f32", lambda p: p.get("block_size", 512)),
-    "matmul": ("gemm", lambda p: 256 if p.get("variant") == "ffma" else 192),
-    "attention": ("fa_fwd", lambda p: 384),
-}
+def kernel_function(kernel: str, p: dict) -> tuple[str, int]:
+    """The __global__ function a variant of `kernel` launches at the tuned size
+    (a substring of its mangled name in the ptxas resource lines) and its block
+    size, for the occupancy analysis."""
+    if kernel in ("softmax", "layernorm"):
+        # stages > 0: the persistent TMA bulk-copy ring kernel; 0: one row per CTA in registers
+        if p.get("stages", 3) > 0:
+            return ("softmax_rows" if kernel == "softmax" else "layernorm_rows"), int(p.get("block_size", 256))
+        return "rows_vec", int(p.get("block_size", 256))
+    if kernel == "reduction":
+        return "sum_f32", int(p.get("block_size", 512))
+    if kernel == "matmul":
+        return ("sgemm_128x128", 256) if p.get("variant") == "ffma" else ("gemm_tf32_kernel", 192)
+    if kernel == "attention":
+        return "fa_fwd_kernel", 480  # 3 producer/MMA warps + 8 softmax warps + 4 epilogue warps
+    raise ValueError(f"unknown kernel {kernel!r}")
 
 
 def results_dir() -> Path:
@@ -328,8 +336,8 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
             res.bound_type = pt.bound_type
             res.roofline_efficiency_pct = pt.efficiency_pct
             res.roofline_ceiling = pt.ceiling_name
-            fn, bs = KERNEL_FUNCTION[kernel]
-            info = occ.analyze_from_stderr(job["log"], fn, bs(p))
+            fn, bs = kernel_function(kernel, p)
+            info = occ.analyze_from_stderr(job["log"], fn, bs)
             if info:
                 res.occupancy = info.occupancy
                 res.registers_per_thread = info.registers_per_thread

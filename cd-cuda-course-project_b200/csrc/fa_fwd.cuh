@@ -41,9 +41,6 @@
 #ifndef KT_FA_VSTAGES
 #define KT_FA_VSTAGES 2
 #endif
-#ifndef KT_FA_BN
-#define KT_FA_BN 128
-#endif
 #ifndef KT_FA_POLY
 #define KT_FA_POLY 0  // 1: every 4th value pair of exponentials on the FMA pipe (measured slower: the FMA/ALU
                       // pipes, not MUFU, limit the softmax warps)
@@ -566,13 +563,8 @@ inline int launch_t(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uin
   if (rc == KT_OK) rc = make_tmap_bhsd(&tv, V, BH, S, D);
   if (rc != KT_OK) return rc;
   auto kern = fa_fwd_kernel<D, KT_FA_STAGES, CAUSAL>;
-  static bool attr_set = false;  // one flag per template instance
-  if (!attr_set) {
-    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES),
-                     "attention: smem attribute");
-    if (rc != KT_OK) return rc;
-    attr_set = true;
-  }
+  rc = ensure_smem((const void*)kern, CF::SMEM_BYTES, "attention: smem attribute");
+  if (rc != KT_OK) return rc;
   const float scale_log2 = scale * 1.4426950408889634f;  // log2(e)
   // persistent: one CTA per SM (TMEM holds one CTA's 512 columns), items strided over the CTAs
   const int64_t items = BH * ((S + BM - 1) / BM);

@@ -261,15 +261,10 @@ inline int launch_t(const float* A, const float* B, float* C, int M, int N, int 
   else rc = make_tmap_2d(&tb, dt, 4, B, (uint64_t)K, (uint64_t)N, (uint64_t)N, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   if (rc != KT_OK) return rc;
   auto kern = gemm_tf32_kernel<BN, STAGES, TB>;
-  static bool attr_set = false;  // per instantiation; the attribute is per-function and idempotent
-  if (!attr_set) {
-    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES),
-                     "gemm tf32: smem attribute");
-    if (rc != KT_OK) return rc;
-    attr_set = true;
-  }
-  const int num_tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = num_tiles < sm_count() ? num_tiles : sm_count();
+  rc = ensure_smem((const void*)kern, CF::SMEM_BYTES, "gemm tf32: smem attribute");
+  if (rc != KT_OK) return rc;
+  const int64_t num_tiles = (((int64_t)M + BM - 1) / BM) * (((int64_t)N + BN - 1) / BN);
+  const int grid = (int)(num_tiles < (int64_t)sm_count() ? num_tiles : (int64_t)sm_count());
   kern<<<grid, THREADS, CF::SMEM_BYTES, st>>>(ta, tb, C, M, N, K);
   return check_launch("gemm tf32");
 }
@@ -287,7 +282,11 @@ inline int launch(const float* A, const float* B, float* C, int64_t M, int64_t N
   // with K == 0 nothing of A or B is read and C = 0
   if (K == 0) return cuda_status(cudaMemsetAsync(C, 0, sizeof(float) * (size_t)M * (size_t)N, st), "gemm: zero C");
   if (!A || !B) return fail(KT_ERR_ARG, "gemm: null pointer");
-  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(KT_ERR_UNSUPPORTED, "gemm tf32: dims >= 2^31");
+  // the kernel counts tiles and k-blocks in int: keep M+BM, N+BN, K+BK and the tile count below 2^31
+  constexpr int64_t kDimMax = (int64_t)INT32_MAX - 1024;
+  if (M > kDimMax || N > kDimMax || K > kDimMax) return fail(KT_ERR_UNSUPPORTED, "gemm tf32: dims >= 2^31 - 1024");
+  if (((M + BM - 1) / BM) * ((N + 63) / 64) > (int64_t)INT32_MAX)
+    return fail(KT_ERR_UNSUPPORTED, "gemm tf32: more than 2^31 output tiles");
   if (!tma_compatible(A, B, N, K, tb)) return gemm_ffma::launch(A, B, C, M, N, K, tb, st);
   if (tb) return launch_t<KT_TC_BN, KT_TC_STAGES, true>(A, B, C, (int)M, (int)N, (int)K, st);
   return launch_t<KT_TC_BN, KT_TC_STAGES, false>(A, B, C, (int)M, (int)N, (int)K, st);

@@ -14,6 +14,8 @@
 #include <string.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "kt_abi.h"
 
 #define KT_ABI_VERSION 1
@@ -53,6 +55,89 @@ inline int sm_count() {
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
   return n > 0 ? n : 148;
+}
+
+// Per-(kernel, device) launch facts that cost a driver call to establish.
+//  * The dynamic shared-memory opt-in (cudaFuncAttributeMaxDynamicSharedMemorySize)
+//    is a property of the function in each device's context, so it is set on
+//    every device the kernel runs on. It only ever grows: lowering it while
+//    another host thread launches the same kernel with more would fail that
+//    launch.
+//  * The resident-CTA count for a (block, smem) launch shape.
+// Lookups and inserts are serialised by one mutex; a full table only repeats
+// the driver calls.
+namespace detail {
+struct FactsTable {
+  struct Smem {
+    const void* fn;
+    int dev;
+    size_t bytes;
+  };
+  struct Occ {
+    const void* fn;
+    int dev;
+    int block;
+    size_t smem;
+    int per_sm;
+  };
+  std::mutex mu;
+  Smem smem[64];
+  int n_smem = 0;
+  Occ occ[64];
+  int n_occ = 0;
+};
+inline FactsTable& facts() {
+  static FactsTable t;
+  return t;
+}
+// Caller holds facts().mu.
+inline int ensure_smem_locked(FactsTable& t, const void* fn, int dev, size_t bytes, const char* what) {
+  if (bytes <= 48 * 1024) return KT_OK;
+  for (int i = 0; i < t.n_smem; ++i)
+    if (t.smem[i].fn == fn && t.smem[i].dev == dev) {
+      if (t.smem[i].bytes >= bytes) return KT_OK;
+      int rc = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes), what);
+      if (rc == KT_OK) t.smem[i].bytes = bytes;
+      return rc;
+    }
+  int rc = cuda_status(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes), what);
+  if (rc == KT_OK && t.n_smem < 64) t.smem[t.n_smem++] = FactsTable::Smem{fn, dev, bytes};
+  return rc;
+}
+}  // namespace detail
+
+// Opt `fn` into `bytes` of dynamic shared memory on the current device.
+inline int ensure_smem(const void* fn, size_t bytes, const char* what) {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), what);
+  if (rc != KT_OK) return rc;
+  detail::FactsTable& t = detail::facts();
+  std::lock_guard<std::mutex> lock(t.mu);
+  return detail::ensure_smem_locked(t, fn, dev, bytes, what);
+}
+
+// ensure_smem, then the number of CTAs of (block, smem) resident per SM.
+inline int resident_ctas(const void* fn, int block, size_t smem, int* per_sm, const char* what) {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), what);
+  if (rc != KT_OK) return rc;
+  detail::FactsTable& t = detail::facts();
+  std::lock_guard<std::mutex> lock(t.mu);
+  rc = detail::ensure_smem_locked(t, fn, dev, smem, what);
+  if (rc != KT_OK) return rc;
+  for (int i = 0; i < t.n_occ; ++i) {
+    const auto& e = t.occ[i];
+    if (e.fn == fn && e.dev == dev && e.block == block && e.smem == smem) {
+      *per_sm = e.per_sm;
+      return KT_OK;
+    }
+  }
+  int n = 0;
+  rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, block, smem), what);
+  if (rc != KT_OK) return rc;
+  if (t.n_occ < 64) t.occ[t.n_occ++] = detail::FactsTable::Occ{fn, dev, block, smem, n};
+  *per_sm = n;
+  return KT_OK;
 }
 
 // ----------------------------------------------------------------------------

@@ -187,11 +187,8 @@ inline int attention(const uint16_t* Q, const uint16_t* K, const uint16_t* V, ui
   if (!Q || !K || !V || !O) return fail(KT_ERR_ARG, "naive attention: null pointer");
   const size_t smem = sizeof(float) * (size_t)S;
   if (smem > 227 * 1024) return fail(KT_ERR_UNSUPPORTED, "naive attention: S too long for the score row");
-  if (smem > 48 * 1024) {
-    int rc = cuda_status(cudaFuncSetAttribute(attention_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                         "naive attention: smem attribute");
-    if (rc != KT_OK) return rc;
-  }
+  int rc = ensure_smem((const void*)attention_rows, smem, "naive attention: smem attribute");
+  if (rc != KT_OK) return rc;
   attention_rows<<<capped_grid(B * H * S), 1, smem, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(Q), reinterpret_cast<const __nv_bfloat16*>(K),
       reinterpret_cast<const __nv_bfloat16*>(V), reinterpret_cast<__nv_bfloat16*>(O), B * H, S, D, scale, causal);

@@ -10,10 +10,13 @@
 // library's own device memory, so nothing is allocated per call.
 //
 // The array lives for as long as the library is loaded, on every device the
-// library is used on. Its address is looked up on the host with
-// cudaGetSymbolAddress once per device (the first call on a device does
-// this, so that first call must not happen inside a stream capture). The
-// ticket word is cleared before each launch; the partials are overwritten.
+// library is used on. Every call looks its device address up on the host with
+// cudaGetSymbolAddress, with the caller's device current (a host-side lookup
+// once the library's device code is loaded; no address is cached, so a
+// cudaDeviceReset or a switch of context cannot leave a stale one). The first
+// call on a device loads that code there, so make the first call outside any
+// stream capture. The ticket word is cleared before each launch; the partials
+// are overwritten.
 // All calls on one device share this one array: two calls whose kernels may
 // overlap on the GPU (different streams, no ordering between them) race and
 // give wrong sums. Serialize such calls on one stream.
@@ -21,8 +24,6 @@
 // This translation unit is included once by kt_entry.cuh, so every built
 // library exports the entry point.
 #pragma once
-
-#include <mutex>
 
 #include "kt_common.cuh"
 #include "reduce.cuh"
@@ -37,27 +38,15 @@ static __device__ __align__(256) unsigned char g_kt_noalloc_scratch[KT_NOALLOC_S
 namespace kt {
 namespace noalloc {
 
-constexpr int kMaxDevices = 64;
-
-// Device address of g_kt_noalloc_scratch on each device, looked up once per
-// device with that device current.
-static void* g_scratch_ptr[kMaxDevices] = {nullptr};
-static std::mutex g_scratch_mu;
-
+// Device address of g_kt_noalloc_scratch on the current device. The name
+// g_kt_noalloc_scratch in host code is only a host-side stand-in; a kernel
+// must be given this address instead.
 inline int scratch_for_current_device(void** out) {
-  int dev = 0;
-  int rc = cuda_status(cudaGetDevice(&dev), "reduce noalloc: cudaGetDevice");
+  void* p = nullptr;
+  int rc = cuda_status(cudaGetSymbolAddress(&p, g_kt_noalloc_scratch), "reduce noalloc: cudaGetSymbolAddress");
   if (rc != KT_OK) return rc;
-  if (dev < 0 || dev >= kMaxDevices) return fail(KT_ERR_UNSUPPORTED, "reduce noalloc: device %d >= %d", dev, kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    rc = cuda_status(cudaGetSymbolAddress(&p, g_kt_noalloc_scratch), "reduce noalloc: cudaGetSymbolAddress");
-    if (rc != KT_OK) return rc;
-    if (p == nullptr) return fail(KT_ERR_CUDA, "reduce noalloc: scratch address is null");
-    g_scratch_ptr[dev] = p;
-  }
-  *out = g_scratch_ptr[dev];
+  if (p == nullptr) return fail(KT_ERR_CUDA, "reduce noalloc: scratch address is null");
+  *out = p;
   return KT_OK;
 }
 

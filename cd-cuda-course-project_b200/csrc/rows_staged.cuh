@@ -171,38 +171,13 @@ layernorm_rows(const float* __restrict__ x, const float* __restrict__ gamma, con
 }
 
 // Grid: as many CTAs as fit (CTAS_PER_SM per SM by shared memory), at most one per row.
-// The attribute + occupancy query is done once per (kernel, shared-memory size)
-// and device; a small table keeps the answers (races only repeat the query).
+// The shared-memory opt-in and the occupancy query are made once per
+// (kernel, launch shape, device) (kt_common.cuh: resident_ctas).
 template <class K>
 inline int launch_grid(K kern, int block, size_t smem, int64_t rows, int* grid_out) {
-  struct Entry {
-    const void* fn;
-    size_t smem;
-    int dev;
-    int per_sm;
-  };
-  static Entry cache[16] = {};
-  int dev = 0;
-  int rc = cuda_status(cudaGetDevice(&dev), "staged rows: device");
-  if (rc != KT_OK) return rc;
   int per_sm = 0;
-  for (const Entry& e : cache)
-    if (e.fn == (const void*)kern && e.smem == smem && e.dev == dev) per_sm = e.per_sm;
-  if (per_sm == 0) {
-    if (smem > 48 * 1024) {
-      rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                       "staged rows: smem attribute");
-      if (rc != KT_OK) return rc;
-    }
-    rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, block, smem),
-                     "staged rows: occupancy");
-    if (rc != KT_OK) return rc;
-    for (Entry& e : cache)
-      if (e.fn == nullptr) {
-        e = Entry{(const void*)kern, smem, dev, per_sm};
-        break;
-      }
-  }
+  int rc = resident_ctas((const void*)kern, block, smem, &per_sm, "staged rows: launch shape");
+  if (rc != KT_OK) return rc;
   if (per_sm < 1) return fail(KT_ERR_UNSUPPORTED, "staged rows: no CTA fits (smem %zu)", smem);
   const int64_t g = (int64_t)sm_count() * per_sm;
   *grid_out = (int)(rows < g ? rows : g);

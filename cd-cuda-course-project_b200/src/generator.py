@@ -57,7 +57,7 @@ MACROS: dict[str, dict[str, str]] = {
                   "stages": "KT_LN_STAGES"},
     "reduction": {"block_size": "KT_REDUCE_BLOCK", "unroll": "KT_REDUCE_UNROLL", "blocks_per_sm": "KT_REDUCE_BPSM"},
     "matmul": {"bk": "KT_FFMA_BK", "cta_tile": "KT_TC_BN", "stages": "KT_TC_STAGES"},
-    "attention": {"kv_tile": "KT_FA_BN", "stages": "KT_FA_STAGES", "v_stages": "KT_FA_VSTAGES",
+    "attention": {"stages": "KT_FA_STAGES", "v_stages": "KT_FA_VSTAGES",
                   "poly_exp2": "KT_FA_POLY"},
 }
 ONLY = {"softmax": "KT_ONLY_SOFTMAX", "layernorm": "KT_ONLY_LAYERNORM", "reduction": "KT_ONLY_REDUCE",

@@ -17,12 +17,14 @@ configurations:
               matmul    fp32 8192×8192×8192, A, B ~ U[-1,1], ±transpose_b
               attention bf16 [8, 32, 4096, 128], Q, K, V ~ N(0,1),
                         scale 1/sqrt(128), causal and non-causal
-All generators use numpy.random.default_rng(seed).
+All generators are numpy.random.default_rng streams seeded per block from
+(seed, family, tensor, block) (see make_inputs).
 """
 
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -102,45 +104,119 @@ def work(kernel: str, d: dict, causal: bool = False, variant: str = "") -> Work:
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
-def make_inputs(kernel: str, size: str = "config", seed: int = DEFAULT_SEED, d: dict | None = None) -> dict:
+# Inputs are drawn in fixed blocks along the sharded dimension, each block from
+# its own generator seeded by (seed, family, tensor, block). Any contiguous
+# part of the batch can therefore be generated alone and matches the same
+# slice of the whole batch, so every rank builds only its shard and the data
+# does not depend on the number of GPUs.
+_BLOCK = {"reduction": 1 << 20, "softmax": 64, "layernorm": 64, "matmul": 64, "attention": 1}
+_TAG = {"softmax": 1, "layernorm": 2, "reduction": 3, "matmul": 4, "attention": 5}
+_PARAMS_BLOCK = 1 << 40  # block id of the per-family parameters (gamma/beta, matmul B)
+
+
+def _rng(seed: int, kernel: str, tensor: int, block: int) -> np.random.Generator:
+    return np.random.default_rng([int(seed), _TAG[kernel], int(tensor), int(block)])
+
+
+def _blocks(kernel: str, seed: int, tensor: int, lo: int, hi: int, row_shape: tuple, dtype, fill_fn) -> np.ndarray:
+    """Units [lo, hi) of the sharded dimension, each unit of shape row_shape,
+    filled block by block (threads: NumPy's generators release the GIL).
+    fill_fn(rng, dst) fills dst in place from rng."""
+    bs = _BLOCK[kernel]
+    out = np.empty((hi - lo, *row_shape), dtype=dtype)
+    if hi <= lo:
+        return out
+    blocks = range(lo // bs, (hi - 1) // bs + 1)
+
+    def fill(b: int) -> None:
+        b0, b1 = b * bs, (b + 1) * bs
+        a0, a1 = max(lo, b0), min(hi, b1)
+        rng = _rng(seed, kernel, tensor, b)
+        if a0 == b0 and a1 == b1:
+            fill_fn(rng, out[a0 - lo:a1 - lo])
+        else:  # a block cut by the part's edge: draw it whole, keep the overlap
+            tmp = np.empty((b1 - b0, *row_shape), dtype=dtype)
+            fill_fn(rng, tmp)
+            out[a0 - lo:a1 - lo] = tmp[a0 - b0:a1 - b0]
+
+    if len(blocks) > 4 and out.nbytes > (8 << 20):
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as ex:
+            list(ex.map(fill, blocks))
+    else:
+        for b in blocks:
+            fill(b)
+    return out
+
+
+def _normal(rng: np.random.Generator, dst: np.ndarray) -> None:
+    rng.standard_normal(out=dst, dtype=np.float32)
+
+
+def _uniform(rng: np.random.Generator, dst: np.ndarray) -> None:
+    rng.random(out=dst, dtype=np.float32)
+    dst *= 2.0
+    dst -= 1.0
+
+
+def _normal_bf16(rng: np.random.Generator, dst: np.ndarray) -> None:
+    f = np.empty(dst.shape, dtype=np.float32)
+    rng.standard_normal(out=f, dtype=np.float32)
+    dst[...] = bf16_bits(f)
+
+
+def shard_unit(kernel: str) -> str:
+    """Name of the dimension a family is sharded along (and `part` counts)."""
+    return {"reduction": "n", "softmax": "rows", "layernorm": "rows", "matmul": "M", "attention": "B*H"}[kernel]
+
+
+def make_inputs(kernel: str, size: str = "config", seed: int = DEFAULT_SEED, d: dict | None = None,
+                part: tuple[int, int] | None = None) -> dict:
     """
     Seeded inputs as numpy arrays (fp32; attention as bf16 bit patterns in
-    uint16 plus their exact fp32 values). `d` overrides the named size.
+    uint16). `d` overrides the named size. `part` = (lo, hi) generates only
+    units [lo, hi) of the sharded dimension (elements, rows, rows of A, or
+    (batch, head) pairs as a [hi-lo, S, D] array), equal to that slice of the
+    whole batch; replicated tensors (gamma, beta, matmul B) are always whole.
     """
     d = dict(d) if d is not None else dims(kernel, size)
-    rng = np.random.default_rng(seed)
-    if kernel == "softmax":
-        return {"x": rng.standard_normal((d["rows"], d["cols"]), dtype=np.float32), **d}
     if kernel == "reduction":
-        return {"x": uniform_pm1(rng, d["n"]), **d}
-    if kernel == "layernorm":
+        n = d["n"]
+        lo, hi = part if part is not None else (0, n)
+        return {"x": _blocks(kernel, seed, 0, lo, hi, (), np.float32, _uniform), **d}
+    if kernel in ("softmax", "layernorm"):
         R, C = d["rows"], d["cols"]
-        x = rng.standard_normal((R, C), dtype=np.float32)
+        lo, hi = part if part is not None else (0, R)
+        x = _blocks(kernel, seed, 0, lo, hi, (C,), np.float32, _normal)
+        if kernel == "softmax":
+            return {"x": x, **d}
+        rng = _rng(seed, kernel, 1, _PARAMS_BLOCK)
         gamma = (1.0 + 0.1 * rng.standard_normal(C)).astype(np.float32)
         beta = (0.1 * rng.standard_normal(C)).astype(np.float32)
         return {"x": x, "gamma": gamma, "beta": beta, "eps": 1e-5, **d}
     if kernel == "matmul":
         M, N, K = d["M"], d["N"], d["K"]
-        A = uniform_pm1(rng, M * K).reshape(M, K)
-        B = uniform_pm1(rng, K * N).reshape(K, N)
+        lo, hi = part if part is not None else (0, M)
+        A = _blocks(kernel, seed, 0, lo, hi, (K,), np.float32, _uniform)
+        B = np.empty((K, N), dtype=np.float32)
+        _uniform(_rng(seed, kernel, 1, _PARAMS_BLOCK), B)
         return {"A": A, "B": B, **d}
     if kernel == "attention":
         B, H, S, D = d["B"], d["H"], d["S"], d["D"]
         out = dict(d)
-        for name in ("q", "k", "v"):
-            f = rng.standard_normal((B, H, S, D), dtype=np.float32)
-            bits = bf16_bits(f)
-            out[name] = bits
+        lo, hi = part if part is not None else (0, B * H)
+        for t, name in enumerate(("q", "k", "v")):
+            bits = _blocks(kernel, seed, t, lo, hi, (S, D), np.uint16, _normal_bf16)
+            out[name] = bits if part is not None else bits.reshape(B, H, S, D)
         out["scale"] = 1.0 / math.sqrt(D)
         return out
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
 def uniform_pm1(rng: np.random.Generator, n: int) -> np.ndarray:
-    """n fp32 values uniform on [-1, 1), drawn natively in fp32 (2^28 values in ~3 s)."""
-    x = rng.random(n, dtype=np.float32)
-    x *= 2.0
-    x -= 1.0
+    """n fp32 values uniform on [-1, 1), drawn natively in fp32."""
+    x = np.empty(n, dtype=np.float32)
+    _uniform(rng, x)
     return x
 
 

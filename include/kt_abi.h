@@ -133,8 +133,10 @@ KT_API int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* ou
  * 16 KiB array (KT_NOALLOC_SCRATCH_BYTES; enough for grids of up to 2046 CTAs)
  * in the library's own device memory, present on every device that uses the
  * library until the process exits; a launch needing more returns
- * KT_ERR_UNSUPPORTED. The first call on a device looks the array up with
- * cudaGetSymbolAddress, so make that first call outside any stream capture.
+ * KT_ERR_UNSUPPORTED. Each call looks the array's device address up with
+ * cudaGetSymbolAddress on the current device; the first call on a device also
+ * loads the library's device code there, so make that first call outside any
+ * stream capture.
  * All calls on a device share the array: calls that may overlap on the GPU
  * (unordered streams) race; order them on one stream.
  * No counterpart in the reference (its executables allocate their own buffers). */

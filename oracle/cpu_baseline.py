@@ -52,14 +52,24 @@ def reduce_sum(x: np.ndarray, threads: int, reps: int = 3) -> dict:
     return {"best_s": best, "median_s": median, "result": out, "bytes": x.nbytes, "threads": threads}
 
 
+def softmax_f32(x: np.ndarray) -> np.ndarray:
+    """Row softmax evaluated in fp32, as the reference's `_ref_softmax` does
+    (src/verifier.py:245-250): subtract the row max, np.exp, divide by the row sum."""
+    e = np.exp(x - x.max(axis=1, keepdims=True))
+    e /= e.sum(axis=1, keepdims=True)
+    return e
+
+
 def rows_op(kind: str, x: np.ndarray, threads: int, reps: int = 3, gamma=None, beta=None, eps: float = 1e-5) -> dict:
-    """Row softmax or LayerNorm (fp64 oracle formulas), rows chunked over threads."""
+    """Row softmax or LayerNorm in the reference's own precision (softmax in
+    fp32, src/verifier.py:245-250; LayerNorm statistics in fp64, :267-274),
+    rows chunked over threads."""
     chunks = np.array_split(np.arange(x.shape[0]), max(1, threads))
 
     def part(idx):
         rows = x[idx[0]:idx[-1] + 1] if idx.size else x[:0]
         if kind == "softmax":
-            return ref.softmax_ref(rows).astype(np.float32)
+            return softmax_f32(rows)
         return ref.layernorm_ref(rows, gamma, beta, eps).astype(np.float32)
 
     with ThreadPoolExecutor(max(1, threads)) as ex:

@@ -121,6 +121,28 @@ def attention_ref(Q: np.ndarray, K: np.ndarray, V: np.ndarray, scale: float | No
     return p @ V64
 
 
+def attention_rows_ref(Q: np.ndarray, K: np.ndarray, V: np.ndarray, rows: np.ndarray, scale: float,
+                       causal: bool = False) -> np.ndarray:
+    """attention_ref for the query rows `rows` of one head ([S, D] arrays) only:
+    the same formula (src/verifier.py:277-294), with the causal mask of the
+    full sequence (key j excluded from query row i when j > i). Lets a test
+    check a long sequence at a fraction of the cost of every row."""
+    rows = np.asarray(rows, dtype=np.int64)
+    K64 = np.asarray(K, dtype=np.float64)
+    V64 = np.asarray(V, dtype=np.float64)
+    out = np.empty((rows.size, K64.shape[-1] if V64.ndim == 2 else V64.shape[-1]), dtype=np.float64)
+    for i0 in range(0, rows.size, 256):
+        r = rows[i0:i0 + 256]
+        s = (np.asarray(Q, dtype=np.float64)[r] @ K64.T) * float(scale)
+        if causal:
+            s = np.where(np.arange(K64.shape[0])[None, :] > r[:, None], -np.inf, s)
+        s = s - s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p = p / p.sum(axis=-1, keepdims=True)
+        out[i0:i0 + r.size] = p @ V64
+    return out
+
+
 # ---------------------------------------------------------------------------
 # bf16 helpers (round-to-nearest-even, as __float2bfloat16_rn)
 # ---------------------------------------------------------------------------

@@ -2,12 +2,13 @@
 make_golden.py — regenerate tests/golden/reference_kat.npz from the reference's
 own NumPy oracle.
 
-It imports `verifier.py` read-only from the reference checkout (default
-/root/reference/src, or $KT_REFERENCE_SRC), calls its `_ref_*` functions at the
+It imports `verifier.py` read-only from the reference checkout's `src/`
+directory, named by the first argument or $KT_REFERENCE_SRC (there is no
+default), calls its `_ref_*` functions at the
 sizes of its verify mains (src/verifier.py:221-294, :542-556) and stores the
 outputs. The reference cannot travel to the GPU machine; these fixtures do.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference-checkout>/src
 """
 
 from __future__ import annotations
@@ -25,7 +26,10 @@ OUT = HERE / "reference_kat.npz"
 
 
 def main() -> None:
-    src = Path(os.environ.get("KT_REFERENCE_SRC", "/root/reference/src"))
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KT_REFERENCE_SRC")
+    if not arg:
+        raise SystemExit("usage: make_golden.py <reference src/ directory> (or set KT_REFERENCE_SRC)")
+    src = Path(arg)
     if not (src / "verifier.py").exists():
         raise SystemExit(f"reference verifier not found under {src}")
     sys.path.insert(0, str(src))

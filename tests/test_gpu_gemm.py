@@ -88,13 +88,17 @@ def test_gemm_tf32_config_size(dev, lib, tb):
     assert lib.device_error() == 0
 
 
-def test_gemm_ffma_config_rows(dev, lib):
+@pytest.mark.parametrize("tb", [False, True])
+def test_gemm_ffma_config_rows(dev, lib, tb):
     inp = workloads.make_inputs("matmul", "config")
-    C = kt_ops.gemm(torch.from_numpy(inp["A"]).to(dev), torch.from_numpy(inp["B"]).to(dev), variant=FFMA, lib=lib)
+    Bh = np.ascontiguousarray(inp["B"].T) if tb else inp["B"]
+    C = kt_ops.gemm(torch.from_numpy(inp["A"]).to(dev), torch.from_numpy(Bh).to(dev), transpose_b=tb, variant=FFMA,
+                    lib=lib)
     torch.cuda.synchronize()
-    rows = np.r_[0:32, 8160:8192]
+    rows = np.r_[0:32, 4000:4032, 8160:8192]
     got = C[torch.from_numpy(rows).to(dev)].cpu().numpy()
     assert ref.normwise_rel_err(got, ref.matmul_ref(inp["A"][rows], inp["B"])) <= 1e-5
+    assert lib.device_error() == 0
 
 
 def test_naive_gemm_matches(dev, lib):

@@ -265,6 +265,31 @@ def test_naive_baselines_match(dev, lib):
     assert abs(out.item() - ref.reduce_sum_ref(x)) <= 1e-3 * abs(ref.reduce_sum_ref(x)) + 1e-3
 
 
+def test_naive_layernorm_matches(dev, lib, golden):
+    """The naive LayerNorm baseline (one thread per row, serial fp32 mean and
+    variance, as src/kernels/baseline_kernels.cu:110-142) against the oracle,
+    on seeded rows with gamma/beta and on the reference's known-answer rows."""
+    inp = workloads.make_inputs("layernorm", d={"rows": 96, "cols": 1024}, seed=21)
+    xd, gd, bd = to_dev(inp["x"], dev), to_dev(inp["gamma"], dev), to_dev(inp["beta"], dev)
+    y = torch.empty_like(xd)
+    lib.run("naive_layernorm", kt_lib.make_args(in0=xd.data_ptr(), in1=gd.data_ptr(), in2=bd.data_ptr(),
+                                                out0=y.data_ptr(), d0=96, d1=1024, f0=inp["eps"]))
+    torch.cuda.synchronize()
+    want = ref.layernorm_ref(inp["x"], inp["gamma"], inp["beta"], inp["eps"])
+    assert ref.normwise_rel_err(y.cpu().numpy(), want) <= 1e-5
+    x = ref.kat_pattern(64).reshape(4, 16)
+    ones, zeros = np.ones(16, np.float32), np.zeros(16, np.float32)
+    xd, gd, bd = to_dev(x, dev), to_dev(ones, dev), to_dev(zeros, dev)
+    y = torch.empty_like(xd)
+    lib.run("naive_layernorm", kt_lib.make_args(in0=xd.data_ptr(), in1=gd.data_ptr(), in2=bd.data_ptr(),
+                                                out0=y.data_ptr(), d0=4, d1=16, f0=1e-5))
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    assert ref.max_abs_diff(got, golden["layernorm_4x16"]) <= golden["tolerances"][3]
+    assert ref.normwise_rel_err(got, ref.layernorm_ref(x, ones, zeros, 1e-5)) <= 1e-5
+    assert lib.device_error() == 0
+
+
 def test_kt_time_samples(dev, lib):
     x = workloads.make_inputs("softmax", "config")["x"]
     xd = to_dev(x, dev)

@@ -98,3 +98,12 @@ def test_planted_reduction_error_is_caught():
 def test_normwise_metric_shape_mismatch():
     assert ref.normwise_rel_err(np.zeros(3), np.ones(3)) == 1.0
     assert ref.normwise_rel_err(np.zeros(0), np.zeros(0)) == 0.0
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_rows_ref_matches_full(causal):
+    rng = np.random.default_rng(4)
+    q, k, v = (rng.standard_normal((300, 64)) for _ in range(3))
+    full = ref.attention_ref(q, k, v, 0.125, causal)
+    rows = np.array([0, 1, 5, 100, 255, 256, 299])
+    assert np.allclose(ref.attention_rows_ref(q, k, v, rows, 0.125, causal), full[rows], rtol=1e-12, atol=1e-14)

@@ -39,25 +39,39 @@ def _noalloc_fn(lib):
 
 
 def test_noalloc_matches_workspace_entry_point_twice(dev, lib):
+    """Two calls queued back to back on one stream (no synchronisation between
+    them), with different lengths and different output buffers; each result is
+    compared with kt_reduce_sum_f32 and with the oracle's fp64 sum."""
+    from oracle import ref
+
     fn = _noalloc_fn(lib)
     stream = torch.cuda.current_stream().cuda_stream
-    for call, (n, seed) in enumerate([((1 << 22) + 3, 101), (1_000_001, 202)]):
+    cases = [((1 << 22) + 3, 101), (1_000_001, 202)]
+    xs, outs = [], []
+    for n, seed in cases:
         x = workloads.make_inputs("reduction", d={"n": n}, seed=seed)["x"]
-        xd = torch.from_numpy(x).to(dev)
-        want64 = kt_ops.reduce_sum(xd, lib=lib).item()
-
-        out64 = torch.full((1,), float("nan"), dtype=torch.float64, device=dev)
-        out32 = torch.full((1,), float("nan"), dtype=torch.float32, device=dev)
-        rc = fn(xd.data_ptr(), n, out64.data_ptr(), out32.data_ptr(), stream)
+        xs.append((x, torch.from_numpy(x).to(dev)))
+        outs.append((torch.full((1,), float("nan"), dtype=torch.float64, device=dev),
+                     torch.full((1,), float("nan"), dtype=torch.float32, device=dev)))
+    torch.cuda.synchronize()
+    for call, ((n, _), (_, xd), (o64, o32)) in enumerate(zip(cases, xs, outs)):
+        rc = fn(xd.data_ptr(), n, o64.data_ptr(), o32.data_ptr(), stream)
         assert rc == 0, f"call {call}: status {rc}: {lib.last_error()}"
-        torch.cuda.synchronize()
-        got64 = out64.item()
+    torch.cuda.synchronize()
+    for call, ((x, xd), (o64, o32)) in enumerate(zip(xs, outs)):
+        got64 = o64.item()
+        want64 = kt_ops.reduce_sum(xd, lib=lib).item()
+        oracle = ref.reduce_sum_ref(x)
         assert abs(got64 - want64) <= 1e-4 * abs(want64), (call, got64, want64)
-        assert float(out32.item()) == float(np.float32(got64))
+        assert abs(got64 - oracle) <= 1e-4 * abs(oracle), (call, got64, oracle)
+        assert float(o32.item()) == float(np.float32(got64))
 
 
 def test_noalloc_rejects_bad_arguments(dev, lib):
     fn = _noalloc_fn(lib)
     xd = torch.zeros(16, device=dev)
+    out64 = torch.zeros(1, dtype=torch.float64, device=dev)
     assert fn(xd.data_ptr(), 16, None, None, None) == 1  # KT_ERR_ARG: null output
-    assert fn(xd.data_ptr(), -1, None, None, None) == 1
+    assert fn(xd.data_ptr(), -1, out64.data_ptr(), None, None) == 1  # negative length
+    assert fn(xd.data_ptr() + 1, 8, out64.data_ptr(), None, None) == 1  # x not 4-byte aligned
+    assert "aligned" in lib.last_error()
