@@ -66,6 +66,7 @@ class Case:
 
 CASES = {c.name: c for c in (
     Case("reduction", "reduction"),
+    Case("reduction_nccl", "reduction", "nccl"),
     Case("softmax", "softmax"),
     Case("layernorm", "layernorm"),
     Case("matmul_tf32", "matmul", "tf32"),
@@ -81,7 +82,8 @@ DEFAULT_FAMILIES = ("softmax", "layernorm", "matmul_tf32", "matmul_tf32_tb", "ma
 # kernel each case's dominant launch runs (matched against the `kernel_id:`
 # line of the committed ncu summaries under profiles/)
 KERNEL_ID = {
-    "reduction": "reduce::sum_f32",
+    "reduction": "reduce::sum_f32_xrank",
+    "reduction_nccl": "reduce::sum_f32",
     "softmax": "staged::softmax_rows",
     "layernorm": "staged::layernorm_rows",
     "matmul_tf32": "gemm_tf32_kernel",
@@ -137,7 +139,11 @@ def family_cases(args: argparse.Namespace, head: Case) -> list[Case]:
     for n in names:
         if n not in CASES:
             raise SystemExit(f"unknown case {n!r}; known: {sorted(CASES)}")
-    return [CASES[n] for n in names if n != head.name]
+    out = [CASES[n] for n in names if n != head.name]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.families == "all" and head.name == "reduction" and world > 1:
+        out.insert(0, CASES["reduction_nccl"])  # the same sum with the partials combined by NCCL, for comparison
+    return out
 
 
 def dist_env() -> tuple[int, int, int]:
@@ -150,8 +156,11 @@ def emit(obj: dict) -> None:
 
 
 def workload_name(c: Case) -> str:
+    if c.kernel == "reduction":
+        how = ("fp64 partials combined by one NCCL all-reduce" if c.variant == "nccl"
+               else "fp64 partials combined inside the kernel over NVLink peer stores")
+        return f"sum reduction fp32 N=2^28 U[-1,1] -> fp64 sum, contiguous shards, {how}"
     return {
-        "reduction": "sum reduction fp32 N=2^28 U[-1,1] -> fp64 sum, contiguous shards + NCCL all-reduce",
         "softmax": "row softmax fp32 4096x4096 N(0,1), rows sharded",
         "layernorm": "layernorm fp32 16384x4096 N(0,1), gamma=1+0.1N, beta=0.1N, eps=1e-5, rows sharded",
         "matmul": f"matmul fp32 8192^3 U[-1,1] {c.variant}{' transpose_b' if c.tb else ''}, row-blocks of A sharded",
@@ -395,7 +404,7 @@ class Job:
     d2h: int
     dev_bytes: int
     parity: Callable[[], dict]
-    collective: Callable[[], None] = lambda: None
+    collective: Optional[Callable[[], None]] = None   # a step's exchange after the kernel (None: none)
     launches_per_step: int = 1
     tensors: list = field(default_factory=list)
 
@@ -436,9 +445,18 @@ def setup_job(ctx: Ctx, c: Case) -> Job:
         out_h = torch.zeros(1, dtype=torch.float64).pin_memory()
         ws_bytes = lib.reduce_workspace_bytes(hi - lo)
         ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+        if c.variant == "nccl":
+            def launch(src):
+                lib.reduce_sum_f32(src.data_ptr(), hi - lo, out64.data_ptr(), None, ws.data_ptr(), ws_bytes, sh)
 
-        def launch(src):
-            lib.reduce_sum_f32(src.data_ptr(), hi - lo, out64.data_ptr(), None, ws.data_ptr(), ws_bytes, sh)
+            collective = lambda: sharding.combine_partials(out64)  # noqa: E731
+        else:
+            xsum = sharding.XrankSum(lib, hi - lo, dev)
+
+            def launch(src):
+                xsum(src.data_ptr(), hi - lo, out64.data_ptr(), sh)
+
+            collective = None
 
         def parity():
             import torch.distributed as dist
@@ -455,7 +473,7 @@ def setup_job(ctx: Ctx, c: Case) -> Job:
 
         return Job(c, d, launch, x_d, x_e, lambda: x_e.copy_(x_h, non_blocking=True),
                    lambda: out_h.copy_(out64, non_blocking=True), n * 4, (hi - lo) * 4, "GB/s", "f32", "hbm",
-                   x_h.numel() * 4, 8, x_d.numel() * 4, parity, collective=lambda: sharding.combine_partials(out64),
+                   x_h.numel() * 4, 8, x_d.numel() * 4, parity, collective=collective,
                    tensors=[x_h, x_d, x_e, out64, out_h, ws])
 
     if c.kernel in ("softmax", "layernorm"):
@@ -653,23 +671,32 @@ def main() -> None:
                 step_fn(ev[i])
             torch.cuda.synchronize()
             barrier()
-            return [a.elapsed_time(b) for a, b, _, _ in ev], [x.elapsed_time(y) for _, _, x, y in ev]
+            step = [a.elapsed_time(b) for a, b, _, _ in ev]
+            if job.collective is None:
+                return step, list(step)
+            return step, [x.elapsed_time(y) for _, _, x, y in ev]
 
+        # A step is bracketed by events e0..e1. With an exchange after the
+        # kernel, a second pair e2..e3 brackets the kernel alone; without one
+        # the kernel is the whole step and its time is e0..e1 (no extra event
+        # records inside the step).
         def dev_step(e):
             e[0].record(stream)
-            e[2].record(stream)
-            job.launch(job.dev_src)
-            e[3].record(stream)
-            job.collective()
+            if job.collective is not None:
+                e[2].record(stream)
+                job.launch(job.dev_src)
+                e[3].record(stream)
+                job.collective()
+            else:
+                job.launch(job.dev_src)
             e[1].record(stream)
 
         def e2e_step(e):
             e[0].record(stream)
             job.e2e_in()
-            e[2].record(stream)
             job.launch(job.e2e_src)
-            e[3].record(stream)
-            job.collective()
+            if job.collective is not None:
+                job.collective()
             job.e2e_out()
             e[1].record(stream)
 

@@ -146,7 +146,8 @@ inline int resident_ctas(const void* fn, int block, size_t smem, int* per_sm, co
 enum DeviceErr : int {
   DEV_OK = 0,
   DEV_MBAR_TIMEOUT = 1,   // an mbarrier wait exceeded its iteration bound
-  DEV_BAD_SHAPE = 2       // a kernel-side bounds check refused an index
+  DEV_BAD_SHAPE = 2,      // a kernel-side bounds check refused an index
+  DEV_XRANK_TIMEOUT = 3   // a cross-GPU exchange wait ran out (a rank never arrived)
 };
 
 }  // namespace kt

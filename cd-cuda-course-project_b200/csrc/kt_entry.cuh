@@ -142,6 +142,17 @@ int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32, vo
 #endif
 }
 
+int kt_reduce_sum_f32_xrank(const float* x, int64_t n, double* out64, float* out32, void* workspace,
+                            size_t ws_bytes, void* const* exchange, int rank, int world, uint64_t epoch,
+                            kt_stream_t stream) {
+  kt::clear_error();
+#if KT_WITH_REDUCE
+  return kt::reduce::launch_xrank(x, n, out64, out32, workspace, ws_bytes, exchange, rank, world, epoch, stream);
+#else
+  return kt::unsupported("reduce");
+#endif
+}
+
 int kt_gemm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int transpose_b,
                 int variant, kt_stream_t stream) {
   kt::clear_error();

@@ -38,6 +38,9 @@ STATUS_NAMES = {
 KT_GEMM_FFMA = 0
 KT_GEMM_TF32 = 1
 
+KT_XRANK_MAX = 8
+KT_XRANK_EXCHANGE_BYTES = 256
+
 OP_IDS = {
     "softmax": 1,
     "layernorm": 2,
@@ -55,6 +58,7 @@ OP_IDS = {
 EXPORTED_SYMBOLS = (
     "kt_last_error", "kt_version", "kt_variant_params",
     "kt_softmax_f32", "kt_layernorm_f32", "kt_reduce_workspace_bytes", "kt_reduce_sum_f32",
+    "kt_reduce_sum_f32_xrank",
     "kt_gemm_f32", "kt_fa_fwd_bf16",
     "kt_naive_softmax_f32", "kt_naive_layernorm_f32", "kt_naive_reduce_sum_f32",
     "kt_naive_gemm_f32", "kt_naive_attention_bf16",
@@ -108,6 +112,8 @@ _SIGNATURES = {
     "kt_layernorm_f32": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "kt_reduce_workspace_bytes": (_size, [_i64]),
     "kt_reduce_sum_f32": (_int, [_vp, _i64, _vp, _vp, _vp, _size, _vp]),
+    "kt_reduce_sum_f32_xrank": (_int, [_vp, _i64, _vp, _vp, _vp, _size, ctypes.POINTER(_vp), _int, _int,
+                                       ctypes.c_uint64, _vp]),
     "kt_gemm_f32": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
     "kt_fa_fwd_bf16": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _int, _vp]),
     "kt_naive_softmax_f32": (_int, [_vp, _vp, _i64, _i64, _vp]),
@@ -176,6 +182,15 @@ class KtLibrary:
                        ws_bytes: int, stream: Optional[int] = None) -> None:
         self._check(self._lib.kt_reduce_sum_f32(x, n, out64, out32, workspace, ws_bytes, stream),
                     "kt_reduce_sum_f32")
+
+    def reduce_sum_f32_xrank(self, x: int, n: int, out64: int, out32: Optional[int], workspace: int,
+                             ws_bytes: int, exchange: Sequence[int], rank: int, world: int, epoch: int,
+                             stream: Optional[int] = None) -> None:
+        """Whole-job sum across `world` ranks (kt_reduce_sum_f32_xrank); `exchange`
+        holds every rank's exchange buffer address as mapped in this process."""
+        arr = (_vp * max(len(exchange), 1))(*[int(p) or None for p in exchange]) if exchange else None
+        self._check(self._lib.kt_reduce_sum_f32_xrank(x, n, out64, out32, workspace, ws_bytes, arr, rank, world,
+                                                      epoch, stream), "kt_reduce_sum_f32_xrank")
 
     def gemm_f32(self, A: int, B: int, C: int, M: int, N: int, K: int, transpose_b: bool,
                  variant: int, stream: Optional[int] = None) -> None:

@@ -2,8 +2,10 @@
 sharding.py — how each family is split across GPUs (one process per GPU).
 
   reduction  contiguous shards of the input; each rank reduces its shard to
-             an fp64 partial on its GPU and the partials are combined by one
-             all-reduce (NCCL over NVLink; gloo in the CPU tests)
+             an fp64 partial on its GPU. The partials are combined inside the
+             reduction kernel itself (XrankSum: peer stores into every rank's
+             exchange buffer over NVLink, kt_reduce_sum_f32_xrank), or by one
+             all-reduce (combine_partials: NCCL, gloo in the CPU tests)
   softmax / layernorm   rows
   matmul     row-blocks of A (B replicated)
   attention  (batch, head) pairs
@@ -42,6 +44,55 @@ def sharded_sum(x_shard, lib=None, group=None, workspace=None, out64=None):
     import kt_ops
     partial = kt_ops.reduce_sum(x_shard, out64=out64, workspace=workspace, lib=lib)
     return combine_partials(partial, group)
+
+
+class XrankSum:
+    """
+    Whole-job sum of per-rank shards with the combine inside the kernel
+    (kt_reduce_sum_f32_xrank): one launch per step and no collective call.
+
+        xs = XrankSum(lib, n_shard, device)          # collective: every rank
+        xs(x_shard_ptr, n_shard, out64_ptr, stream)  # every rank, every step
+
+    Set-up allocates each rank's exchange buffer with torch's symmetric memory
+    (peer mappings over NVLink; multicast objects are not requested), zeroes it
+    and the workspace, and agrees on them with a barrier. `epoch` counts calls
+    (identical on every rank, since all ranks call once per step).
+    """
+
+    def __init__(self, lib, n_shard: int, device, group=None):
+        import os
+        import torch
+        import torch.distributed as dist
+        import kt_lib
+
+        self.lib = lib
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        if self.world > kt_lib.KT_XRANK_MAX:
+            raise ValueError(f"XrankSum supports up to {kt_lib.KT_XRANK_MAX} ranks, not {self.world}")
+        self.ws_bytes = max(lib.reduce_workspace_bytes(n_shard), 16)
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=device)  # ticket starts at zero
+        self.ptrs: list[int] = []
+        self._buf = self._hdl = None
+        if self.world > 1:
+            os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+            import torch.distributed._symmetric_memory as symm_mem
+            g = group if group is not None else dist.group.WORLD
+            self._buf = symm_mem.empty(kt_lib.KT_XRANK_EXCHANGE_BYTES, dtype=torch.uint8, device=device)
+            self._buf.zero_()
+            self._hdl = symm_mem.rendezvous(self._buf, g)
+            self.ptrs = [int(p) for p in self._hdl.buffer_ptrs]
+            if len(self.ptrs) != self.world or self.ptrs[self.rank] != self._buf.data_ptr():
+                raise RuntimeError("symmetric-memory rendezvous returned an unexpected buffer table")
+            torch.cuda.synchronize(device)
+            dist.barrier(group=g, device_ids=[device.index])
+        self.epoch = 0
+
+    def __call__(self, x: int, n: int, out64: int, stream, out32: Optional[int] = None) -> None:
+        self.epoch += 1
+        self.lib.reduce_sum_f32_xrank(x, n, out64, out32, self.ws.data_ptr(), self.ws_bytes, self.ptrs,
+                                      self.rank, self.world, self.epoch, stream)
 
 
 class RankLostError(RuntimeError):

@@ -126,6 +126,33 @@ KT_API size_t kt_reduce_workspace_bytes(int64_t n);
 KT_API int kt_reduce_sum_f32(const float* x, int64_t n, double* out64, float* out32,
                       void* workspace, size_t ws_bytes, kt_stream_t stream);
 
+/* Whole-job sum over `world` GPUs, one process per GPU, each holding one
+ * contiguous shard of the input: every rank calls this once per step with its
+ * shard and gets the sum of all shards (fp64, identical bits on every rank) in
+ * *out64 (and *out32 if not NULL). The combine runs inside the kernel: the last
+ * CTA of each rank stores its fp64 shard sum into every rank's exchange buffer
+ * over NVLink (plain peer stores) and adds the `world` values in rank order
+ * once all have arrived. No collective library is called. The wait for the
+ * other ranks is bounded (2 s); when it runs out *out64 is NaN and
+ * kt_device_error reports 3.
+ *   workspace  as kt_reduce_sum_f32 (>= kt_reduce_workspace_bytes(n)), but its
+ *              first 4 bytes must be zero before the first call on it (the
+ *              kernel leaves them zero), so no per-call reset is issued.
+ *   exchange   host array of `world` device pointers: exchange[r] is rank r's
+ *              exchange buffer (KT_XRANK_EXCHANGE_BYTES, zeroed before the first
+ *              call, 16-byte aligned) as mapped into this process (CUDA IPC or
+ *              any symmetric-memory mapping); may be NULL when world == 1.
+ *   epoch      1 for the first call on these buffers, +1 for every later call;
+ *              all ranks pass the same value.
+ * world <= KT_XRANK_MAX. Replaces the per-GPU partial + ncclAllReduce(sum) of
+ * one fp64 that a sharded `reduction_opt` would need; the reference's own
+ * kernel (src/generator.py:82-98) runs on one GPU only. */
+#define KT_XRANK_MAX 8
+#define KT_XRANK_EXCHANGE_BYTES 256
+KT_API int kt_reduce_sum_f32_xrank(const float* x, int64_t n, double* out64, float* out32,
+                                   void* workspace, size_t ws_bytes, void* const* exchange,
+                                   int rank, int world, uint64_t epoch, kt_stream_t stream);
+
 /* Same result as kt_reduce_sum_f32, for callers that cannot allocate device
  * memory (host callbacks and real-time loops where cudaMalloc would block or
  * synchronize, embedders with a fixed memory budget, FFI callers holding only

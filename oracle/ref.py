@@ -179,6 +179,20 @@ def normwise_rel_err(got: np.ndarray, ref: np.ndarray) -> float:
     return num / denom if denom > 0 else num
 
 
+def product_scaled_err(got: np.ndarray, A: np.ndarray, B: np.ndarray) -> float:
+    """max|C - A·B| / max(|A|·|B|): the error of a matmul measured against the
+    magnitude of its products. Rounding each operand to tf32 (10 explicit
+    mantissa bits) moves every product by at most ~2^-10 of its size, so this
+    ratio stays below 1e-3 even when a short dot product cancels to a small
+    value, where max|C - A·B| / max|A·B| need not."""
+    A64 = np.asarray(A, dtype=np.float64)
+    B64 = np.asarray(B, dtype=np.float64)
+    exact = A64 @ B64
+    scale = float(np.max(np.abs(A64) @ np.abs(B64))) if exact.size else 0.0
+    num = float(np.max(np.abs(np.asarray(got, dtype=np.float64) - exact))) if exact.size else 0.0
+    return num / scale if scale > 0 else num
+
+
 def max_abs_diff(got: np.ndarray, ref: np.ndarray) -> float:
     """The reference's metric: max absolute difference (src/verifier.py:558-569)."""
     g = np.asarray(got, dtype=np.float64).ravel()

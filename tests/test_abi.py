@@ -55,6 +55,14 @@ def test_null_and_negative_arguments_are_rejected(lib):
         lambda: lib.gemm_f32(0, 0, 0, -8, 8, 8, False, kt_lib.KT_GEMM_FFMA),
         lambda: lib.gemm_f32(1 << 20, 1 << 20, 1 << 20, 8, 8, 8, False, 7),
         lambda: lib.fa_fwd_bf16(0, 0, 0, 0, 1, 1, 128, 128, 0.1, False),
+        # cross-GPU sum: bad world / rank / epoch / exchange table, all refused before any CUDA call
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 1 << 20, None, 1 << 20, 1 << 16, [], 0, 0, 1),
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 1 << 20, None, 1 << 20, 1 << 16, [1 << 20] * 9, 0, 9, 1),
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 1 << 20, None, 1 << 20, 1 << 16, [1 << 20] * 2, 2, 2, 1),
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 1 << 20, None, 1 << 20, 1 << 16, [1 << 20] * 2, 0, 2, 0),
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 1 << 20, None, 1 << 20, 1 << 16, [1 << 20, 0], 0, 2, 1),
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 1 << 20, None, 1 << 20, 1 << 16, [1 << 20, 8], 0, 2, 1),
+        lambda: lib.reduce_sum_f32_xrank(1 << 20, 16, 0, None, 1 << 20, 1 << 16, [], 0, 1, 1),
     ]
     for fn in checks:
         with pytest.raises(kt_lib.KtError) as ei:

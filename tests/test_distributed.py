@@ -104,3 +104,27 @@ def test_rank_loss_is_detected_between_steps():
     assert out[1][1] == "left"
     assert out[0][1] == "detected", out[0]
     assert out[0][2] == [1] and out[0][3] == 3
+
+
+def test_xrank_sum_counts_epochs_on_one_rank():
+    """XrankSum without a process group: one rank, no exchange table, and the
+    epoch passed to the kernel entry point starts at 1 and grows by one per call."""
+    import sharding
+
+    class FakeLib:
+        def __init__(self):
+            self.calls = []
+
+        def reduce_workspace_bytes(self, n):
+            return 16 + 8 * 4
+
+        def reduce_sum_f32_xrank(self, x, n, out64, out32, ws, ws_bytes, exchange, rank, world, epoch, stream):
+            self.calls.append((x, n, out64, ws_bytes, list(exchange), rank, world, epoch))
+
+    lib = FakeLib()
+    xs = sharding.XrankSum(lib, 1000, "cpu")
+    assert int(xs.ws.sum()) == 0 and xs.ws_bytes == 48
+    xs(111, 1000, 222, None)
+    xs(111, 1000, 222, None)
+    assert [c[-1] for c in lib.calls] == [1, 2]
+    assert all(c[4] == [] and c[5] == 0 and c[6] == 1 for c in lib.calls)

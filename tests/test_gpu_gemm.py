@@ -4,7 +4,9 @@ kernel and the TF32 tcgen05 kernel, with and without transpose_b, against
 the fp64 oracle.
 
 Tolerances: FFMA normwise max|C-ref|/max|ref| <= 1e-5; TF32 normwise <= 1e-3
-(BASELINE budget for tf32 operands). On the reference's known-answer inputs
+(the budget for tf32 operands); for TF32 with K < 32 the error is measured
+against max(|A|·|B|) instead (oracle.ref.product_scaled_err), since a short
+dot product may cancel. On the reference's known-answer inputs
 (N=64) the FFMA path also meets the reference's max-abs budget 1e-3
 (src/verifier.py:47-53).
 """
@@ -57,7 +59,12 @@ def test_gemm_shapes(dev, lib, variant, tb, M, N, K):
     inp = workloads.make_inputs("matmul", d={"M": M, "N": N, "K": K}, seed=M * 7 + N * 3 + K)
     C = run(lib, dev, inp["A"], inp["B"], tb, variant)
     assert C.shape == (M, N)
-    assert ref.normwise_rel_err(C, ref.matmul_ref(inp["A"], inp["B"])) <= TOL[variant]
+    if variant == TF32 and K < 32:
+        # a dot product of a few terms can cancel to a value far below its
+        # products; tf32 rounding is bounded relative to the products
+        assert ref.product_scaled_err(C, inp["A"], inp["B"]) <= TOL[variant]
+    else:
+        assert ref.normwise_rel_err(C, ref.matmul_ref(inp["A"], inp["B"])) <= TOL[variant]
     assert lib.device_error() == 0
 
 
