@@ -34,12 +34,19 @@
 #pragma once
 #include "kt_common.cuh"
 #include "sm100.cuh"
+#include "fa_fwd2.cuh"
 
 #ifndef KT_FA_STAGES
 #define KT_FA_STAGES 2  // K ring depth (the V ring has KT_FA_VSTAGES slots)
 #endif
 #ifndef KT_FA_VSTAGES
 #define KT_FA_VSTAGES 2
+#endif
+#ifndef KT_FA_KIND
+#define KT_FA_KIND 1  // 1: one query tile per CTA (this file); 2: two ping-pong query tiles per CTA (fa_fwd2.cuh)
+#endif
+#ifndef KT_FA_EXP16
+#define KT_FA_EXP16 0  // 1: exponentials as packed half-precision pairs (ex2.approx.f16x2: two results per MUFU op)
 #endif
 #ifndef KT_FA_POLY
 #define KT_FA_POLY 0  // 1: every 4th value pair of exponentials on the FMA pipe (measured slower: the FMA/ALU
@@ -103,6 +110,20 @@ __device__ __forceinline__ float ex2_poly(float x) {
   p = fmaf(p, f, 0.9999513626098633f);
   const int ni = __float_as_int(y) - 0x4B400000;  // bits of 1.5·2^23
   return __int_as_float(__float_as_int(p) + (ni << 23));
+}
+
+// 2^x0, 2^x1 from one packed half-precision MUFU operation. The arguments are
+// rounded to fp16 first (for |x| < 16 the rounding moves 2^x by at most 0.3 %,
+// below the 0.4 % of the bf16 rounding that P gets anyway; values below 2^-24
+// flush to 0, negligible against a row sum >= 1) and the results come back as
+// fp32 for the row sum.
+__device__ __forceinline__ void ex2_h2(float x0, float x1, float& p0, float& p1) {
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(p0), "=f"(p1)
+      : "r"(e));
 }
 
 // Pack two fp32 values into bf16x2 (round to nearest even); `lo` in the low half.
@@ -460,7 +481,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             const float x0 = fmaf(__uint_as_float(sv[c + 2 * i]), scale_log2, -m_run);
             const float x1 = fmaf(__uint_as_float(sv[c + 2 * i + 1]), scale_log2, -m_run);
             float p0, p1;
-            if (KT_FA_POLY && !mask_tile && (i & 3) == 3) {
+            if (KT_FA_EXP16) {
+              ex2_h2(x0, x1, p0, p1);
+            } else if (KT_FA_POLY && !mask_tile && (i & 3) == 3) {
               p0 = ex2_poly(x0);
               p1 = ex2_poly(x1);
             } else {
@@ -587,6 +610,14 @@ inline int launch(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint1
     return fail(KT_ERR_UNSUPPORTED, "attention: S or B*H too large");
   if (!(scale > 0.f) || !isfinite(scale)) return fail(KT_ERR_ARG, "attention: scale must be finite and > 0");
   const int64_t BH = B * H;
+  if (KT_FA_KIND == 2) {
+    // two ping-pong query tiles per CTA (fa_fwd2.cuh)
+    if (D == 128)
+      return causal ? fa2::launch_t<128, true>(Q, K, V, O, BH, S, scale, st)
+                    : fa2::launch_t<128, false>(Q, K, V, O, BH, S, scale, st);
+    return causal ? fa2::launch_t<64, true>(Q, K, V, O, BH, S, scale, st)
+                  : fa2::launch_t<64, false>(Q, K, V, O, BH, S, scale, st);
+  }
   if (D == 128) {
     return causal ? launch_t<128, true>(Q, K, V, O, BH, S, scale, st) : launch_t<128, false>(Q, K, V, O, BH, S, scale, st);
   }

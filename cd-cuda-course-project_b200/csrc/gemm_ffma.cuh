@@ -18,6 +18,9 @@
 #ifndef KT_FFMA_MINB
 #define KT_FFMA_MINB 2
 #endif
+#ifndef KT_FFMA_X2
+#define KT_FFMA_X2 0  // 0: scalar FFMA (sgemm_128x128); 1: packed fma.rn.f32x2 kernel (sgemm_x2_128x128), measured slower
+#endif
 
 namespace kt {
 namespace gemm_ffma {
@@ -156,10 +159,167 @@ sgemm_128x128(const float* __restrict__ A, const float* __restrict__ B, float* _
   }
 }
 
+// ---------------------------------------------------------------------------
+// Packed variant: the same 128x128 CTA tile and 8x8 outputs per thread, with
+// the FMAs issued as fma.rn.f32x2 (two fp32 FMAs per lane per instruction, a
+// Blackwell instruction). Each packed FMA updates two outputs of one row:
+//   {c[i][j], c[i][j+1]} += {a[i], a[i]} * {b[j], b[j+1]}
+// so A is kept in shared memory with every value stored twice ({a, a} pairs)
+// and both operands come out of 128-bit shared loads ready to use. One k step
+// is 32 packed FMAs and 6 shared loads per thread, against 64 FMAs and 4 loads
+// in sgemm_128x128: half the issue slots for the same FMA-pipe work. Every
+// output is still one fp32 fma.rn per k in k-ascending order, so results are
+// bit-identical to sgemm_128x128.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fma2(unsigned long long& c, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(a), "l"(b));
+}
+
+template <int BK>
+struct X2Smem {
+  static constexpr int A_ROW = 2 * BM + 4;  // floats per k row of the duplicated A tile (16-byte multiple)
+  static constexpr int B_ROW = BN + 4;
+  static constexpr int A_FLOATS = 2 * BK * A_ROW;  // two buffers
+  static constexpr int B_FLOATS = 2 * BK * B_ROW;
+  static constexpr size_t BYTES = sizeof(float) * (size_t)(A_FLOATS + B_FLOATS);
+};
+
+template <bool TB, bool VEC, int BK, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB)
+sgemm_x2_128x128(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int64_t M,
+                 int64_t N, int64_t K) {
+  static_assert(BK == 8 || BK == 16 || BK == 32, "BK");
+  using SM = X2Smem<BK>;
+  extern __shared__ __align__(16) float x2_smem[];
+  float* As = x2_smem;                  // [2][BK][A_ROW]: {a, a} pairs, k-major
+  float* Bs = x2_smem + SM::A_FLOATS;   // [2][BK][B_ROW], k-major
+  constexpr int AV = BM * BK / 4 / THREADS;
+  constexpr int BV = BN * BK / 4 / THREADS;
+  static_assert(AV >= 1 && BV >= 1, "tile/threads");
+  constexpr int KQ = BK / 4;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+
+  float4 ra[AV], rb[BV];
+  auto load_tile = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < AV; ++i) {
+      const int e = tid + i * THREADS;
+      const int r = e / KQ, kq = (e % KQ) * 4;
+      ra[i] = load4<VEC>(A, m0 + r, k0 + kq, M, K, K);
+    }
+#pragma unroll
+    for (int i = 0; i < BV; ++i) {
+      const int e = tid + i * THREADS;
+      if (TB) {
+        const int r = e / KQ, kq = (e % KQ) * 4;
+        rb[i] = load4<VEC>(B, n0 + r, k0 + kq, N, K, K);
+      } else {
+        const int kr = e / (BN / 4), nq = (e % (BN / 4)) * 4;
+        rb[i] = load4<VEC>(B, k0 + kr, n0 + nq, K, N, N);
+      }
+    }
+  };
+  auto store_tile = [&](int buf) {
+    float* as = As + buf * BK * SM::A_ROW;
+    float* bs = Bs + buf * BK * SM::B_ROW;
+#pragma unroll
+    for (int i = 0; i < AV; ++i) {
+      const int e = tid + i * THREADS;
+      const int r = e / KQ, kq = (e % KQ) * 4;
+      *reinterpret_cast<float2*>(&as[(kq + 0) * SM::A_ROW + 2 * r]) = make_float2(ra[i].x, ra[i].x);
+      *reinterpret_cast<float2*>(&as[(kq + 1) * SM::A_ROW + 2 * r]) = make_float2(ra[i].y, ra[i].y);
+      *reinterpret_cast<float2*>(&as[(kq + 2) * SM::A_ROW + 2 * r]) = make_float2(ra[i].z, ra[i].z);
+      *reinterpret_cast<float2*>(&as[(kq + 3) * SM::A_ROW + 2 * r]) = make_float2(ra[i].w, ra[i].w);
+    }
+#pragma unroll
+    for (int i = 0; i < BV; ++i) {
+      const int e = tid + i * THREADS;
+      if (TB) {
+        const int r = e / KQ, kq = (e % KQ) * 4;
+        bs[(kq + 0) * SM::B_ROW + r] = rb[i].x;
+        bs[(kq + 1) * SM::B_ROW + r] = rb[i].y;
+        bs[(kq + 2) * SM::B_ROW + r] = rb[i].z;
+        bs[(kq + 3) * SM::B_ROW + r] = rb[i].w;
+      } else {
+        const int kr = e / (BN / 4), nq = (e % (BN / 4)) * 4;
+        *reinterpret_cast<float4*>(&bs[kr * SM::B_ROW + nq]) = rb[i];
+      }
+    }
+  };
+
+  // acc[i][p] = {c[row i][col 2p], c[row i][col 2p+1]} over this thread's 8 rows x 8 columns
+  unsigned long long acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) acc[i][p] = 0ull;
+
+  const int64_t nk = (K + BK - 1) / BK;
+  load_tile(0);
+  store_tile(0);
+  __syncthreads();
+  for (int64_t t = 0; t < nk; ++t) {
+    const int cur = (int)(t & 1);
+    if (t + 1 < nk) load_tile((t + 1) * BK);
+    const float* as = As + cur * BK * SM::A_ROW;
+    const float* bs = Bs + cur * BK * SM::B_ROW;
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      const ulonglong2 a0 = *reinterpret_cast<const ulonglong2*>(&as[k * SM::A_ROW + 2 * (ty * 4)]);
+      const ulonglong2 a1 = *reinterpret_cast<const ulonglong2*>(&as[k * SM::A_ROW + 2 * (ty * 4) + 4]);
+      const ulonglong2 a2 = *reinterpret_cast<const ulonglong2*>(&as[k * SM::A_ROW + 2 * (64 + ty * 4)]);
+      const ulonglong2 a3 = *reinterpret_cast<const ulonglong2*>(&as[k * SM::A_ROW + 2 * (64 + ty * 4) + 4]);
+      const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(&bs[k * SM::B_ROW + tx * 4]);
+      const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(&bs[k * SM::B_ROW + 64 + tx * 4]);
+      const unsigned long long a[8] = {a0.x, a0.y, a1.x, a1.y, a2.x, a2.y, a3.x, a3.y};
+      const unsigned long long b[4] = {b0.x, b0.y, b1.x, b1.y};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int p = 0; p < 4; ++p) fma2(acc[i][p], a[i], b[p]);
+    }
+    if (t + 1 < nk) store_tile(cur ^ 1);
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (row >= M) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t col = n0 + h * 64 + tx * 4;
+      float* c = C + row * N + col;
+      const float2 lo = *reinterpret_cast<const float2*>(&acc[i][2 * h]);
+      const float2 hi = *reinterpret_cast<const float2*>(&acc[i][2 * h + 1]);
+      const float4 v = make_float4(lo.x, lo.y, hi.x, hi.y);
+      if (VEC && col + 3 < N) {
+        *reinterpret_cast<float4*>(c) = v;
+      } else {
+        if (col + 0 < N) c[0] = v.x;
+        if (col + 1 < N) c[1] = v.y;
+        if (col + 2 < N) c[2] = v.z;
+        if (col + 3 < N) c[3] = v.w;
+      }
+    }
+  }
+}
+
 template <bool TB, bool VEC>
-inline void launch_t(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+inline int launch_t(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  sgemm_128x128<TB, VEC, KT_FFMA_BK, KT_FFMA_MINB><<<grid, THREADS, 0, st>>>(A, B, C, M, N, K);
+  if constexpr (KT_FFMA_X2 != 0) {
+    auto kern = sgemm_x2_128x128<TB, VEC, KT_FFMA_BK, KT_FFMA_MINB>;
+    constexpr size_t smem = X2Smem<KT_FFMA_BK>::BYTES;
+    int rc = ensure_smem((const void*)kern, smem, "gemm ffma: smem attribute");
+    if (rc != KT_OK) return rc;
+    kern<<<grid, THREADS, smem, st>>>(A, B, C, M, N, K);
+  } else {
+    sgemm_128x128<TB, VEC, KT_FFMA_BK, KT_FFMA_MINB><<<grid, THREADS, 0, st>>>(A, B, C, M, N, K);
+  }
+  return KT_OK;
 }
 
 inline int launch(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int tb,
@@ -173,13 +333,10 @@ inline int launch(const float* A, const float* B, float* C, int64_t M, int64_t N
   if ((M + BM - 1) / BM > 65535) return fail(KT_ERR_UNSUPPORTED, "gemm: M too large for the grid");
   const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && (K % 4 == 0) && (tb ? true : (N % 4 == 0)) &&
                    (N % 4 == 0);
-  if (tb) {
-    if (vec) launch_t<true, true>(A, B, C, M, N, K, st);
-    else launch_t<true, false>(A, B, C, M, N, K, st);
-  } else {
-    if (vec) launch_t<false, true>(A, B, C, M, N, K, st);
-    else launch_t<false, false>(A, B, C, M, N, K, st);
-  }
+  int rc;
+  if (tb) rc = vec ? launch_t<true, true>(A, B, C, M, N, K, st) : launch_t<true, false>(A, B, C, M, N, K, st);
+  else rc = vec ? launch_t<false, true>(A, B, C, M, N, K, st) : launch_t<false, false>(A, B, C, M, N, K, st);
+  if (rc != KT_OK) return rc;
   return check_launch("gemm ffma");
 }
 

@@ -13,11 +13,14 @@ Blackwell axes the sm_100a kernels actually expose:
   reduction:
       block_size, unroll (16-byte loads in flight per thread), blocks_per_sm
   matmul:
-      variant {ffma, tf32}, transpose_b; ffma: bk (k tile);
+      variant {ffma, tf32}, transpose_b; ffma: bk (k tile), ffma_x2 (packed
+      fma.rn.f32x2 kernel), min_blocks (register budget: CTAs per SM);
       tf32 (tcgen05): cta_tile (M×N of the TMEM accumulator), stages (TMA
-      pipeline depth), tma_box (k extent of one TMA box)
-  attention (tcgen05): stages (K ring depth), v_stages (V ring depth),
-      poly_exp2 (FMA-pipe exponentials)
+      pipeline depth)
+  attention (tcgen05): kind (1: one query tile per CTA, 2: two ping-pong
+      query tiles), stages / v_stages (K / V ring depth) and poly_exp2 for
+      kind 1, order (MMA issue order) and poly_every (FMA-pipe exponential
+      share) for kind 2
 
 Each axis is a template parameter of the kernel source (see generator.py),
 so every point of the space compiles to a distinct kernel. The reference's
@@ -211,12 +214,17 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["variant"] = ["tf32", "ffma"]
         space["transpose_b"] = [False, True]
         space["bk"] = [8, 16, 32]
+        space["ffma_x2"] = [0, 1]         # ffma: packed fma.rn.f32x2 (two fp32 FMAs per lane per instruction)
+        space["min_blocks"] = [1, 2]      # ffma: resident CTAs per SM asked of the register allocator
         space["cta_tile"] = ["128x128", "128x256"]
         space["stages"] = [3, 4, 5, 6]
     elif fam == "attention":
-        space["stages"] = [1, 2, 3]       # K ring depth
-        space["v_stages"] = [1, 2, 3]     # V ring depth
-        space["poly_exp2"] = [0, 1]       # share of exponentials on the FMA pipe
+        space["kind"] = [1, 2]            # 1: one 128-row query tile per CTA; 2: two ping-pong query tiles
+        space["stages"] = [1, 2, 3]       # kind 1: K ring depth
+        space["v_stages"] = [1, 2, 3]     # kind 1: V ring depth
+        space["poly_exp2"] = [0, 1]       # kind 1: every 4th exponential pair on the FMA pipe
+        space["order"] = [0, 1]           # kind 2: MMA issue order (0 ping-pong, 1 in phase)
+        space["poly_every"] = [0, 4, 8]   # kind 2: every n-th exponential pair on the FMA pipe (0: none)
         space["causal"] = [False, True]
     else:
         space["block_size"] = [64, 128, 192, 256]
@@ -251,10 +259,19 @@ def is_valid(kernel: str, params: dict) -> bool:
         return params.get("block_size", 512) * params.get("blocks_per_sm", 1) <= 2048
     if fam == "matmul":
         if params.get("variant") == "ffma":
-            # the FFMA kernel ignores the tcgen05 axes: keep one representative point
+            # the FFMA kernels ignore the tcgen05 axes: keep one representative point; the scalar
+            # kernel's static shared tiles exceed 48 KB at bk=32
+            if params.get("bk", 16) == 32 and not params.get("ffma_x2", 1):
+                return False
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
-        return params.get("bk", 16) == 16
+        # the tcgen05 kernel ignores the FFMA axes
+        return params.get("bk", 16) == 16 and params.get("ffma_x2", 1) == 1 and params.get("min_blocks", 2) == 2
     if fam == "attention":
+        if params.get("kind", 1) == 2:
+            # the kind-1 axes do not shape this kernel: one representative point
+            return (params.get("stages", 2), params.get("v_stages", 2), params.get("poly_exp2", 0)) == (2, 2, 0)
+        if params.get("order", 0) != 0 or params.get("poly_every", 0) != 0:
+            return False
         # head dim 128: two Q buffers + (K + V slots) x 32 KB must fit the 227 KB of shared memory
         return params.get("stages", 2) + params.get("v_stages", 2) <= 4
     return True
