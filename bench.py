@@ -662,7 +662,7 @@ def main() -> None:
             if flush_needed:
                 torch.sum(flush_buf, dim=0, keepdim=True, out=flush_sink)
 
-        def timed(step_fn, steps: int):
+        def timed(step_fn, steps: int, inner: bool = True):
             ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(4)) for _ in range(steps)]
             barrier()
             torch.cuda.synchronize()
@@ -672,7 +672,7 @@ def main() -> None:
             torch.cuda.synchronize()
             barrier()
             step = [a.elapsed_time(b) for a, b, _, _ in ev]
-            if job.collective is None:
+            if job.collective is None or not inner:
                 return step, list(step)
             return step, [x.elapsed_time(y) for _, _, x, y in ev]
 
@@ -726,7 +726,7 @@ def main() -> None:
                 e2e_step(dummy)
             torch.cuda.synchronize()
             e_steps = max(3, min(args.steps, 50))
-            e_ms, _ = timed(e2e_step, e_steps)
+            e_ms, _ = timed(e2e_step, e_steps, inner=False)
             e_total = max_over_ranks(sum(e_ms))
             e2e = {"value": job.units_job * e_steps / (e_total * 1e-3) / scale_u, "unit": job.unit,
                    "h2d_bytes_per_step": int(sum_over_ranks(job.h2d)),

@@ -134,3 +134,22 @@ def test_naive_attention_matches(dev, lib):
         torch.cuda.synchronize()
         got = workloads.bf16_to_f32(o.view(torch.int16).cpu().numpy().view(np.uint16))
         assert ref.normwise_rel_err(got, oracle(inp["q"], inp["k"], inp["v"], inp["scale"], causal)) <= TOL
+
+
+@pytest.mark.parametrize("params", [{"kind": 2, "order": 0}, {"kind": 2, "order": 1, "exp16": 1},
+                                    {"kind": 1, "exp16": 1}, {"kind": 1, "poly_exp2": 1}])
+def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
+    """Non-default kernels of the tuner's attention axes, built as variant
+    libraries: the two-query-tile ping-pong kernel (both MMA issue orders) and
+    the half-precision / polynomial exponentials, against the oracle."""
+    monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
+    import generator
+    ok, log, so = generator.ensure_variant("attention", params)
+    assert ok, log
+    v = kt_lib.KtLibrary(so)
+    for (B, H, S, D) in ((1, 2, 1000, 128), (2, 3, 300, 64), (1, 1, 77, 128), (4, 40, 300, 64)):
+        inp = workloads.make_inputs("attention", d={"B": B, "H": H, "S": S, "D": D}, seed=S + D + H)
+        for causal in (False, True):
+            o = run(v, dev, inp["q"], inp["k"], inp["v"], inp["scale"], causal)
+            assert ref.normwise_rel_err(o, oracle(inp["q"], inp["k"], inp["v"], inp["scale"], causal)) <= TOL
+    assert v.device_error() == 0

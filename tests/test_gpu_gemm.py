@@ -133,3 +133,19 @@ def test_two_variant_libraries_in_one_process(dev, lib, tmp_path, monkeypatch):
         for tb in (False, True):
             C = run(L, dev, inp["A"], inp["B"], tb, TF32)
             assert ref.normwise_rel_err(C, want) <= 1e-3
+
+
+def test_gemm_ffma_packed_variant(dev, lib, tmp_path, monkeypatch):
+    """The packed fma.rn.f32x2 FFMA kernel (tuner axis ffma_x2), built as a
+    variant library: exact fp32 like the default, on ragged and aligned shapes."""
+    monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
+    import generator
+    ok, log, so = generator.ensure_variant("matmul", {"variant": "ffma", "bk": 16, "ffma_x2": 1, "min_blocks": 1})
+    assert ok, log
+    v = kt_lib.KtLibrary(so)
+    for (M, N, K) in ((129, 257, 33), (512, 384, 1024), (7, 260, 12)):
+        inp = workloads.make_inputs("matmul", d={"M": M, "N": N, "K": K}, seed=M + N + K)
+        for tb in (False, True):
+            C = run(v, dev, inp["A"], inp["B"], tb, FFMA)
+            assert ref.normwise_rel_err(C, ref.matmul_ref(inp["A"], inp["B"])) <= 1e-5
+    assert v.device_error() == 0
