@@ -79,19 +79,20 @@ CASES = {c.name: c for c in (
 DEFAULT_FAMILIES = ("softmax", "layernorm", "matmul_tf32", "matmul_tf32_tb", "matmul_ffma", "attention",
                     "attention_causal")
 
-# kernel each case's dominant launch runs (matched against the `kernel_id:`
-# line of the committed ncu summaries under profiles/)
+# kernel instance (name<template arguments>) each case's dominant launch runs
+# with the default library, matched against the `kernel_id:` line of the
+# committed ncu summaries under profiles/
 KERNEL_ID = {
-    "reduction": "reduce::sum_f32_xrank",
-    "reduction_nccl": "reduce::sum_f32",
-    "softmax": "staged::softmax_rows",
-    "layernorm": "staged::layernorm_rows",
-    "matmul_tf32": "gemm_tf32_kernel",
-    "matmul_tf32_tb": "gemm_tf32_kernel",
-    "matmul_ffma": "sgemm_128x128",
-    "matmul_ffma_tb": "sgemm_128x128",
-    "attention": "fa_fwd_kernel",
-    "attention_causal": "fa_fwd_kernel",
+    "reduction": "sum_f32_xrank<512,4>",
+    "reduction_nccl": "sum_f32<512,4>",
+    "softmax": "softmax_rows<256,4,3>",
+    "layernorm": "layernorm_rows<256,4,3>",
+    "matmul_tf32": "gemm_tf32_kernel<256,4,0>",
+    "matmul_tf32_tb": "gemm_tf32_kernel<256,4,1>",
+    "matmul_ffma": "sgemm_128x128<0,1,16,2>",
+    "matmul_ffma_tb": "sgemm_128x128<1,1,16,2>",
+    "attention": "fa_fwd_kernel<128,2,0>",
+    "attention_causal": "fa_fwd_kernel<128,2,1>",
 }
 
 

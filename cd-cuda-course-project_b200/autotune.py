@@ -64,7 +64,10 @@ def kernel_function(kernel: str, p: dict) -> tuple[str, int]:
     (a substring of its mangled name in the ptxas resource lines) and its block
     size, for the occupancy analysis."""
     if kernel in ("softmax", "layernorm"):
-        # stages > 0: the persistent TMA bulk-copy ring kernel; 0: one row per CTA in registers
+        # cluster_size > 1: rows split across a cluster; stages > 0: the persistent TMA
+        # bulk-copy ring kernel; 0: one row per CTA in registers
+        if p.get("cluster_size", 1) > 1:
+            return "rows_kernel", int(p.get("block_size", 256))
         if p.get("stages", 3) > 0:
             return ("softmax_rows" if kernel == "softmax" else "layernorm_rows"), int(p.get("block_size", 256))
         return "rows_vec", int(p.get("block_size", 256))

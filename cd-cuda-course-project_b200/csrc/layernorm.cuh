@@ -13,6 +13,7 @@
 #pragma once
 #include "kt_common.cuh"
 #include "rows_staged.cuh"
+#include "rows_cluster.cuh"
 
 #ifndef KT_LN_BLOCK
 #define KT_LN_BLOCK 256
@@ -22,6 +23,9 @@
 #endif
 #ifndef KT_LN_MINB
 #define KT_LN_MINB 1
+#endif
+#ifndef KT_LN_CLUSTER
+#define KT_LN_CLUSTER 1  // > 1: every row split across a cluster of this many CTAs (rows_cluster.cuh)
 #endif
 #ifndef KT_LN_STAGES
 #define KT_LN_STAGES 3  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
@@ -210,7 +214,11 @@ inline int launch(const float* x, const float* gamma, const float* beta, float* 
   constexpr int BLOCK = KT_LN_BLOCK;
   constexpr int VPT = KT_LN_VPT;
   constexpr int CAP = BLOCK * VPT * 4;
+  constexpr int CST = KT_LN_STAGES > 0 ? KT_LN_STAGES : 2;  // chunk ring depth of the cluster kernel
   const unsigned g = (unsigned)(rows < max_grid ? rows : max_grid);
+  const bool al = (c & 3) == 0 && aligned16(x) && aligned16(y) && aligned16(gamma) && aligned16(beta);
+  if (KT_LN_CLUSTER > 1 && al && clustered::fits<BLOCK, VPT, CST>(KT_LN_CLUSTER, c))
+    return clustered::launch<BLOCK, VPT, CST, 1>(KT_LN_CLUSTER, x, gamma, beta, y, rows, c, eps, KT_ROWS_BOX, st);
   if (c <= CAP) {
     if ((c & 3) == 0 && aligned16(x) && aligned16(y) && aligned16(gamma) && aligned16(beta)) {
       if (KT_LN_STAGES > 0 && staged::smem_bytes<(KT_LN_STAGES > 0 ? KT_LN_STAGES : 1)>(c) <= 200 * 1024) {
@@ -228,6 +236,11 @@ inline int launch(const float* x, const float* gamma, const float* beta, float* 
     }
     rows_scalar<BLOCK, VPT * 4><<<g, BLOCK, 0, st>>>(x, gamma, beta, y, rows, c, eps);
     return check_launch("layernorm rows_scalar");
+  }
+  // wider than one CTA holds: split each row across a cluster when the chunks fit
+  if (al) {
+    const int C = clustered::smallest_fit<BLOCK, VPT, CST>(c);
+    if (C > 0) return clustered::launch<BLOCK, VPT, CST, 1>(C, x, gamma, beta, y, rows, c, eps, KT_ROWS_BOX, st);
   }
   rows_stream<BLOCK><<<g, BLOCK, 0, st>>>(x, gamma, beta, y, rows, cols, eps);
   return check_launch("layernorm rows_stream");

@@ -17,8 +17,25 @@
 #include "kt_common.cuh"
 #include "sm100.cuh"
 
+#ifndef KT_ROWS_BOX
+#define KT_ROWS_BOX 0  // bytes per bulk copy of a row (a multiple of 16); 0: the whole row in one copy
+#endif
+static_assert(KT_ROWS_BOX % 16 == 0, "bulk copies move multiples of 16 bytes");
+
 namespace kt {
 namespace staged {
+
+// Copy one row into a slot as bulk copies of at most KT_ROWS_BOX bytes each
+// (0: one copy), all completing on the slot's mbarrier.
+__device__ __forceinline__ void load_row(uint32_t dst, const float* src, uint32_t bytes, uint32_t bar) {
+  using namespace sm100;
+  mbar_arrive_expect_tx(bar, bytes);
+  const uint32_t piece = KT_ROWS_BOX == 0 ? bytes : (uint32_t)KT_ROWS_BOX;
+  for (uint32_t off = 0; off < bytes; off += piece) {
+    const uint32_t n = bytes - off < piece ? bytes - off : piece;
+    bulk_load(dst + off, reinterpret_cast<const uint8_t*>(src) + off, n, bar);
+  }
+}
 
 // Shared-memory layout: STAGES row slots of `cols` floats (16-byte aligned),
 // then STAGES mbarriers.
@@ -45,8 +62,7 @@ __device__ __forceinline__ bool for_each_row(const float* __restrict__ x, int64_
     fence_mbar_init();
     for (int s = 0; s < STAGES && s < count; ++s) {
       const int64_t row = blockIdx.x + (int64_t)s * gridDim.x;
-      mbar_arrive_expect_tx(bar0 + 8u * s, row_bytes);
-      bulk_load(slot0 + s * row_bytes, x + row * cols, row_bytes, bar0 + 8u * s);
+      load_row(slot0 + s * row_bytes, x + row * cols, row_bytes, bar0 + 8u * s);
     }
   }
   __syncthreads();
@@ -71,8 +87,7 @@ __device__ __forceinline__ bool for_each_row(const float* __restrict__ x, int64_
     if (threadIdx.x == 0 && k + STAGES < count) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads before the async write
       const int64_t row = blockIdx.x + (k + STAGES) * gridDim.x;
-      mbar_arrive_expect_tx(bar0 + 8u * s, row_bytes);
-      bulk_load(slot0 + s * row_bytes, x + row * cols, row_bytes, bar0 + 8u * s);
+      load_row(slot0 + s * row_bytes, x + row * cols, row_bytes, bar0 + 8u * s);
     }
     body(v, blockIdx.x + k * gridDim.x);
   }

@@ -12,13 +12,18 @@
 //                  template makes 3 global passes (5·R·C·4 bytes).
 //   * rows_scalar— same, for rows whose start is not 16-byte aligned.
 //   * rows_warp  — one warp per row for short rows (cols <= 512).
-//   * rows_stream— rows longer than the register capacity: one online
+//   * clustered  — rows_cluster.cuh: each row split across a thread-block
+//                  cluster (DSMEM exchange of partial max / sum), one read + one
+//                  write for rows up to 8x the register capacity; also a tuner
+//                  option (cluster_size) for rows that one CTA could hold.
+//   * rows_stream— rows longer than that, or not 16-byte aligned: one online
 //                  (max, sum) pass, then one normalising pass (2 reads + 1 write).
 // expf is CUDA's accurate expf (no fast-math); the result is scaled by the
 // reciprocal of the row sum.
 #pragma once
 #include "kt_common.cuh"
 #include "rows_staged.cuh"
+#include "rows_cluster.cuh"
 
 #ifndef KT_SOFTMAX_BLOCK
 #define KT_SOFTMAX_BLOCK 256
@@ -28,6 +33,9 @@
 #endif
 #ifndef KT_SOFTMAX_MINB
 #define KT_SOFTMAX_MINB 1
+#endif
+#ifndef KT_SOFTMAX_CLUSTER
+#define KT_SOFTMAX_CLUSTER 1  // > 1: every row split across a cluster of this many CTAs (rows_cluster.cuh)
 #endif
 #ifndef KT_SOFTMAX_STAGES
 #define KT_SOFTMAX_STAGES 3  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
@@ -209,7 +217,12 @@ inline int launch(const float* x, float* y, int64_t rows, int64_t cols, cudaStre
   constexpr int BLOCK = KT_SOFTMAX_BLOCK;
   constexpr int VPT = KT_SOFTMAX_VPT;
   constexpr int CAP = BLOCK * VPT * 4;
+  constexpr int CST = KT_SOFTMAX_STAGES > 0 ? KT_SOFTMAX_STAGES : 2;  // chunk ring depth of the cluster kernel
   const unsigned g = (unsigned)(rows < max_grid ? rows : max_grid);
+  const bool al = (c & 3) == 0 && aligned16(x) && aligned16(y);
+  if (KT_SOFTMAX_CLUSTER > 1 && al && clustered::fits<BLOCK, VPT, CST>(KT_SOFTMAX_CLUSTER, c))
+    return clustered::launch<BLOCK, VPT, CST, 0>(KT_SOFTMAX_CLUSTER, x, nullptr, nullptr, y, rows, c, 0.f,
+                                                 KT_ROWS_BOX, st);
   if (c <= CAP) {
     if ((c & 3) == 0 && aligned16(x) && aligned16(y)) {
       if (KT_SOFTMAX_STAGES > 0 && staged::smem_bytes<(KT_SOFTMAX_STAGES > 0 ? KT_SOFTMAX_STAGES : 1)>(c) <= 200 * 1024) {
@@ -227,6 +240,11 @@ inline int launch(const float* x, float* y, int64_t rows, int64_t cols, cudaStre
     }
     rows_scalar<BLOCK, VPT * 4><<<g, BLOCK, 0, st>>>(x, y, rows, c);
     return check_launch("softmax rows_scalar");
+  }
+  // wider than one CTA holds: split each row across a cluster when the chunks fit
+  if (al) {
+    const int C = clustered::smallest_fit<BLOCK, VPT, CST>(c);
+    if (C > 0) return clustered::launch<BLOCK, VPT, CST, 0>(C, x, nullptr, nullptr, y, rows, c, 0.f, KT_ROWS_BOX, st);
   }
   rows_stream<BLOCK><<<g, BLOCK, 0, st>>>(x, y, rows, cols);
   return check_launch("softmax rows_stream");

@@ -52,9 +52,9 @@ def variants_dir() -> Path:
 # parameter -> macro, per family; parameters absent here are runtime arguments
 MACROS: dict[str, dict[str, str]] = {
     "softmax": {"block_size": "KT_SOFTMAX_BLOCK", "vec_per_thread": "KT_SOFTMAX_VPT", "min_blocks": "KT_SOFTMAX_MINB",
-                "stages": "KT_SOFTMAX_STAGES"},
+                "stages": "KT_SOFTMAX_STAGES", "cluster_size": "KT_SOFTMAX_CLUSTER", "tma_box": "KT_ROWS_BOX"},
     "layernorm": {"block_size": "KT_LN_BLOCK", "vec_per_thread": "KT_LN_VPT", "min_blocks": "KT_LN_MINB",
-                  "stages": "KT_LN_STAGES"},
+                  "stages": "KT_LN_STAGES", "cluster_size": "KT_LN_CLUSTER", "tma_box": "KT_ROWS_BOX"},
     "reduction": {"block_size": "KT_REDUCE_BLOCK", "unroll": "KT_REDUCE_UNROLL", "blocks_per_sm": "KT_REDUCE_BPSM"},
     "matmul": {"bk": "KT_FFMA_BK", "ffma_x2": "KT_FFMA_X2", "min_blocks": "KT_FFMA_MINB",
                "cta_tile": "KT_TC_BN", "stages": "KT_TC_STAGES"},

@@ -9,7 +9,10 @@ Blackwell axes the sm_100a kernels actually expose:
   memory-bound rows (softmax, layernorm):
       block_size, vec_per_thread (128-bit loads per thread, i.e. the row
       capacity held in registers), min_blocks (occupancy hint), stages
-      (rows in flight per CTA through a TMA bulk-copy ring; 0 = register kernel)
+      (rows in flight per CTA through a TMA bulk-copy ring; 0 = register kernel),
+      cluster_size (CTAs of a thread-block cluster that split every row and
+      exchange partial statistics through distributed shared memory),
+      tma_box (bytes per bulk copy of a row or chunk; 0 = one copy)
   reduction:
       block_size, unroll (16-byte loads in flight per thread), blocks_per_sm
   matmul:
@@ -206,6 +209,8 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["vec_per_thread"] = [1, 2, 4, 8]
         space["min_blocks"] = [1, 2, 4]
         space["stages"] = [0, 2, 3, 4]    # 0: one row per CTA in registers; n: TMA bulk-copy ring of n rows
+        space["cluster_size"] = [1, 2, 4]  # CTAs of a thread-block cluster sharing each row (DSMEM exchange)
+        space["tma_box"] = [0, 4096, 8192]  # bytes per bulk copy of a row or chunk (0: one copy)
     elif fam == "reduction":
         space["block_size"] = [256, 512, 1024]
         space["unroll"] = [2, 4, 8]
@@ -254,6 +259,8 @@ def is_valid(kernel: str, params: dict) -> bool:
     if fam in ("softmax", "layernorm"):
         if params.get("stages", 0) > 0 and params.get("min_blocks", 1) != 1:
             return False  # the staged kernel sizes its grid by occupancy; min_blocks only shapes the register kernel
+        if params.get("tma_box", 0) and params.get("stages", 3) == 0 and params.get("cluster_size", 1) == 1:
+            return False  # the register kernel makes no bulk copies
         return params.get("block_size", 256) * params.get("min_blocks", 1) <= 2048
     if fam == "reduction":
         return params.get("block_size", 512) * params.get("blocks_per_sm", 1) <= 2048

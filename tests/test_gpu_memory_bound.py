@@ -321,3 +321,50 @@ def test_register_kernel_variant(dev, lib, tmp_path, monkeypatch, fam):
             y = kt_ops.layernorm(to_dev(inp["x"], dev), to_dev(inp["gamma"], dev), to_dev(inp["beta"], dev),
                                  inp["eps"], lib=v).cpu().numpy()
             layernorm_ok(y, inp["x"], inp["gamma"], inp["beta"], inp["eps"])
+
+
+# ---------------------------------------------------------------------------
+# Rows split across a thread-block cluster (DSMEM exchange of partials)
+# ---------------------------------------------------------------------------
+
+# wider than one CTA's 4096-float capacity: the default library splits each row
+# across a cluster of 2 (8192), 4 (12288, 16384) or 8 (32768) CTAs; 8196 and
+# 40000 have no such split and take the two-pass streaming kernel
+WIDE = [(37, 8192), (300, 8192), (5, 12288), (19, 16384), (3, 32768), (2, 8196), (2, 40000)]
+
+
+@pytest.mark.parametrize("rows,cols", WIDE)
+def test_wide_rows(dev, lib, rows, cols):
+    inp = workloads.make_inputs("layernorm", d={"rows": rows, "cols": cols}, seed=rows * 13 + cols)
+    y = kt_ops.softmax(to_dev(inp["x"], dev), lib=lib).cpu().numpy()
+    softmax_ok(y, inp["x"])
+    y = kt_ops.layernorm(to_dev(inp["x"], dev), to_dev(inp["gamma"], dev), to_dev(inp["beta"], dev), inp["eps"],
+                         lib=lib).cpu().numpy()
+    layernorm_ok(y, inp["x"], inp["gamma"], inp["beta"], inp["eps"])
+    assert lib.device_error() == 0
+
+
+@pytest.mark.parametrize("fam", ["softmax", "layernorm"])
+@pytest.mark.parametrize("params", [{"cluster_size": 2}, {"cluster_size": 4, "tma_box": 4096},
+                                    {"stages": 3, "tma_box": 4096}])
+def test_cluster_and_box_variants(dev, lib, tmp_path, monkeypatch, fam, params):
+    """Tuner points of the Blackwell axes, built as variant libraries: rows that
+    one CTA could hold split across a cluster of 2 or 4 CTAs, and bulk copies
+    cut into 4 KB pieces (the staged ring and the cluster kernel)."""
+    monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
+    import generator
+    full = {"block_size": 256, "vec_per_thread": 4, "min_blocks": 1, "stages": 3, **params}
+    ok, log, so = generator.ensure_variant(fam, full)
+    assert ok, log
+    v = kt_lib.KtLibrary(so)
+    assert v.variant_params().get("cluster_size", 1) == params.get("cluster_size", 1)
+    for rows, cols in ((257, 4096), (4, 1024), (3, 2056), (4096, 4096)):
+        inp = workloads.make_inputs(fam, d={"rows": rows, "cols": cols}, seed=rows + 3 * cols)
+        if fam == "softmax":
+            y = kt_ops.softmax(to_dev(inp["x"], dev), lib=v).cpu().numpy()
+            softmax_ok(y, inp["x"])
+        else:
+            y = kt_ops.layernorm(to_dev(inp["x"], dev), to_dev(inp["gamma"], dev), to_dev(inp["beta"], dev),
+                                 inp["eps"], lib=v).cpu().numpy()
+            layernorm_ok(y, inp["x"], inp["gamma"], inp["beta"], inp["eps"])
+    assert v.device_error() == 0

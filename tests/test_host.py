@@ -70,7 +70,8 @@ def _space():
 def _objective(p):
     # smooth synthetic latency, minimum at block 256, vec 4, min_blocks 1, stages 3
     return (1.0 + (math.log2(p["block_size"]) - 8) ** 2 + (math.log2(p["vec_per_thread"]) - 2) ** 2
-            + 0.5 * math.log2(p["min_blocks"]) ** 2 + 0.25 * (p["stages"] - 3) ** 2)
+            + 0.5 * math.log2(p["min_blocks"]) ** 2 + 0.25 * (p["stages"] - 3) ** 2
+            + 0.3 * math.log2(p.get("cluster_size", 1)) + 0.1 * p.get("tma_box", 0) / 4096)
 
 
 def test_grid_strategy_covers_valid_points():
@@ -81,7 +82,8 @@ def test_grid_strategy_covers_valid_points():
     assert all(kparser.is_valid("softmax", p) for p in pts)
     for p in pts:
         g.update(p, _objective(p))
-    assert g.best() == {"block_size": 256, "vec_per_thread": 4, "min_blocks": 1, "stages": 3}
+    assert g.best() == {"block_size": 256, "vec_per_thread": 4, "min_blocks": 1, "stages": 3, "cluster_size": 1,
+                        "tma_box": 0}
 
 
 def test_bayesian_strategy_finds_optimum_within_budget():
