@@ -85,8 +85,8 @@ DEFAULT_FAMILIES = ("softmax", "layernorm", "matmul_tf32", "matmul_tf32_tb", "ma
 KERNEL_ID = {
     "reduction": "sum_f32_xrank<512,4>",
     "reduction_nccl": "sum_f32<512,4>",
-    "softmax": "softmax_rows<256,4,3>",
-    "layernorm": "layernorm_rows<256,4,3>",
+    "softmax": "softmax_rows<256,4,2>",
+    "layernorm": "layernorm_rows<256,4,2>",
     "matmul_tf32": "gemm_tf32_kernel<256,4,0>",
     "matmul_tf32_tb": "gemm_tf32_kernel<256,4,1>",
     "matmul_ffma": "sgemm_128x128<0,1,16,2>",

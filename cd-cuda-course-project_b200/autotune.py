@@ -6,6 +6,7 @@ autotune.py — the tuner's command line (B200, sm_100a).
     python autotune.py --kernel=reduction --strategy=sha --gpus=8
     python autotune.py --baseline-only
     python autotune.py --kernel=matmul --skip-verification --workers=8
+    python autotune.py --kernel=all --strategy=sha --budget=8 --compile-only   # host cores only
 
 Same flags as the reference's CLI (autotune.py:596-640: --kernel, --baseline-only,
 --workers, --warmup, --samples, --iters, --strategy, --skip-verification,
@@ -59,6 +60,47 @@ from search import ConvergenceLogger, make_strategy  # noqa: E402
 SUPPORTED_KERNELS = list(FAMILIES)
 RECYCLE_AFTER = 48  # variant libraries loaded per worker before it is replaced
 
+def work_scale(kernel: str, dims: dict, p: dict) -> float:
+    """Work of the family's reference problem over the work of this point's
+    problem: runtime axes that change the amount of work (the causal mask
+    halves attention's) must not make a point look faster. Layout axes
+    (transpose_b) keep the work and give 1."""
+    import workloads
+    if kernel == "attention" and p.get("causal"):
+        d = {k: dims[k] for k in ("B", "H", "S", "D")}
+        return workloads.work("attention", d, causal=False).flops / workloads.work("attention", d, causal=True).flops
+    return 1.0
+
+
+def launch_resources(kernel: str, p: dict, dims: dict) -> tuple[int, int]:
+    """(dynamic shared memory bytes, TMEM columns) one CTA of the point's kernel
+    takes at the tuned problem size, for the occupancy analysis (ptxas reports
+    only static shared memory). Mirrors the Cfg/smem_bytes formulas of csrc/."""
+    if kernel in ("softmax", "layernorm"):
+        cols = int(dims.get("cols", 4096))
+        c = int(p.get("cluster_size", 1))
+        st = int(p.get("stages", 3))
+        if c > 1:
+            return (st if st > 0 else 2) * (cols // c) * 4 + (st if st > 0 else 2) * 8 + 16, 0
+        return (st * cols * 4 + st * 8 + 16 if st > 0 else 0), 0
+    if kernel == "matmul":
+        if p.get("variant") == "ffma":
+            if int(p.get("ffma_x2", 0)):
+                bk = int(p.get("bk", 16))
+                return 4 * 2 * bk * ((2 * 128 + 4) + (128 + 4)), 0
+            return 0, 0
+        bn = int(str(p.get("cta_tile", "128x256")).split("x")[1])
+        stages = int(p.get("stages", 4))
+        return stages * (128 * 32 + bn * 32) * 4 + 1024 + 256, 2 * bn
+    if kernel == "attention":
+        d = int(dims.get("D", 128))
+        if p.get("kind", 1) == 2:
+            return 2 * 128 * d * 2 + 8 * 64 * d * 2 + 1024 + 2048, 512
+        st, vst = int(p.get("stages", 2)), int(p.get("v_stages", 2))
+        return (2 + st + vst) * 128 * d * 2 + 4096 + 1024 + 256, 512
+    return 0, 0
+
+
 def kernel_function(kernel: str, p: dict) -> tuple[str, int]:
     """The __global__ function a variant of `kernel` launches at the tuned size
     (a substring of its mangled name in the ptxas resource lines) and its block
@@ -76,7 +118,13 @@ def kernel_function(kernel: str, p: dict) -> tuple[str, int]:
     if kernel == "matmul":
         return ("sgemm_128x128", 256) if p.get("variant") == "ffma" else ("gemm_tf32_kernel", 192)
     if kernel == "attention":
-        return "fa_fwd_kernel", 480  # 3 producer/MMA warps + 8 softmax warps + 4 epilogue warps
+        # the library holds D=64 and D=128 instances; the tuned size has D=128
+        c = int(bool(p.get("causal")))
+        if p.get("kind", 1) == 2:
+            # loaders, MMA lane, 2 x 4 softmax warps, 4 epilogue warps
+            return f"fa2_fwd_kernelILi128ELi4ELi4ELb{c}", 512
+        # 3 loader/MMA warps + 8 softmax warps + 4 epilogue warps
+        return f"fa_fwd_kernelILi128ELi{int(p.get('stages', 2))}ELb{c}", 480
     raise ValueError(f"unknown kernel {kernel!r}")
 
 
@@ -340,7 +388,8 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
             res.roofline_efficiency_pct = pt.efficiency_pct
             res.roofline_ceiling = pt.ceiling_name
             fn, bs = kernel_function(kernel, p)
-            info = occ.analyze_from_stderr(job["log"], fn, bs)
+            dyn, tmem = launch_resources(kernel, p, r["dims"])
+            info = occ.analyze_from_stderr(job["log"], fn, bs, dynamic_smem_bytes=dyn, tmem_columns=tmem)
             if info:
                 res.occupancy = info.occupancy
                 res.registers_per_thread = info.registers_per_thread
@@ -348,11 +397,12 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
                 res.has_register_spill = info.has_register_spill
                 res.spill_stores = info.spill_stores
                 res.spill_loads = info.spill_loads
+            res.normalized_ms = mean * work_scale(kernel, r["dims"], p)
             results.append(res)
-            strategy.update(p, mean)
-            conv.record(p, mean)
+            strategy.update(p, res.normalized_ms)
+            conv.record(p, res.normalized_ms)
         n_eval += len(batch)
-        best = min(results, key=lambda x: x.mean_ms) if results else None
+        best = min(results, key=lambda x: x.normalized_ms) if results else None
         elapsed = time.time() - t0
         print(f"  [{n_eval:4d}] best {best.mean_ms:.4f} ms ({best.roofline_efficiency_pct:.1f}% roofline)"
               if best else f"  [{n_eval:4d}] no passing variant yet", f" {elapsed:.0f}s")
@@ -365,7 +415,7 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
                         "speedup": round(x.speedup, 3) if x.speedup else None, "passed": x.is_significant}
                        for x in sorted(results, key=lambda x: x.mean_ms)[:5]],
         }, indent=2))
-    results.sort(key=lambda x: x.mean_ms)
+    results.sort(key=lambda x: x.normalized_ms)
     conv.save()
     (rdir / f"{kernel}_failures.json").write_text(json.dumps(failures, indent=2))
     (rdir / f"{kernel}_tuning.json").write_text(json.dumps({
@@ -393,6 +443,31 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
     return results
 
 
+def compile_only(kernels: list[str], strategy_name: str, budget: Optional[int], seed: int, workers: int) -> int:
+    """Generate and nvcc the variants each strategy suggests first, on host cores.
+
+    Grid and successive halving suggest their whole first round up front (later
+    halving rounds re-time a subset of it), so every library those runs load is
+    built here; the Bayesian strategy's first batch only. Returns 0 when every
+    variant compiled."""
+    failed = 0
+    for k in kernels:
+        space = build_search_space(build_kernel_profile(k))
+        strategy = make_strategy(strategy_name, space, kernel=k, n_calls=budget or 40, n_configs=budget or 80,
+                                 seed=seed)
+        pts = strategy.suggest(1 << 30)
+        keys = {compile_key(k, p): p for p in pts}
+        t0 = time.time()
+        with ThreadPoolExecutor(max_workers=workers) as ex:
+            built = list(ex.map(lambda p: ensure_variant(k, p), keys.values()))
+        bad = [key for key, (ok, _, _) in zip(keys, built) if not ok]
+        failed += len(bad)
+        print(f"[COMPILE] {k}: {len(keys)} libraries for {len(pts)} points in {time.time() - t0:.0f}s"
+              + (f", {len(bad)} failed: {bad}" if bad else ""))
+    print(f"[DONE] libraries in {results_dir() / 'variants'}")
+    return 0 if failed == 0 else 1
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description="Kernel auto-tuner — NVIDIA B200 (sm_100a)")
     ap.add_argument("--kernel", choices=SUPPORTED_KERNELS + ["all"], default="matmul")
@@ -414,11 +489,17 @@ def main(argv=None) -> int:
     ap.add_argument("--budget", type=int, default=None, help="max evaluations (bayesian) / initial configs (sha)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--results-dir", default=None)
+    ap.add_argument("--compile-only", action="store_true",
+                    help="only generate and compile the variants the strategy starts with (no GPU needed); a later "
+                         "run with the same --results-dir, strategy, budget and seed reuses the libraries")
     a = ap.parse_args(argv)
     if a.results_dir:
         os.environ["KT_RESULTS_DIR"] = a.results_dir
     n_samples = a.iters if a.iters is not None else a.samples
     kernels = SUPPORTED_KERNELS if a.kernel == "all" else [a.kernel]
+
+    if a.compile_only:
+        return compile_only(kernels, a.strategy, a.budget, a.seed, a.workers)
 
     print("[BASELINE] naive GPU kernels ...")
     baselines = run_baseline_benchmark(a.warmup, n_samples, kernels=kernels, size=a.size)

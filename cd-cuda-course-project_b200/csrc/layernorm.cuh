@@ -28,7 +28,7 @@
 #define KT_LN_CLUSTER 1  // > 1: every row split across a cluster of this many CTAs (rows_cluster.cuh)
 #endif
 #ifndef KT_LN_STAGES
-#define KT_LN_STAGES 3  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
+#define KT_LN_STAGES 2  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
 #endif
 
 namespace kt {

@@ -156,7 +156,7 @@ template <int BLOCK, int UNROLL>
 __global__ void __launch_bounds__(BLOCK)
 sum_f32_xrank(const float* __restrict__ x, int64_t n, int head, double* __restrict__ partials,
               unsigned int* __restrict__ ticket, double* __restrict__ out64, float* __restrict__ out32,
-              XrankPeers peers, int rank, int world, unsigned long long epoch) {
+              const __grid_constant__ XrankPeers peers, int rank, int world, unsigned long long epoch) {
   __shared__ double red[32];
   __shared__ double vals[KT_XRANK_MAX];
   __shared__ int timed_out;
@@ -166,13 +166,23 @@ sum_f32_xrank(const float* __restrict__ x, int64_t n, int head, double* __restri
   if (threadIdx.x == 0) timed_out = 0;
   const int phase = (int)(epoch & 1ull);
   __syncthreads();
+  // peers is a __grid_constant__ parameter read with compile-time indices, so
+  // no thread copies the pointer table to local memory (a by-value parameter
+  // indexed at run time was copied by every thread of every CTA)
+  XrankSlot* to_peer = nullptr;
+  XrankSlot* own = nullptr;
+#pragma unroll
+  for (int r = 0; r < KT_XRANK_MAX; ++r) {
+    if ((int)threadIdx.x == r) to_peer = peers.p[r];
+    if (rank == r) own = peers.p[r];
+  }
   if (world > 1 && threadIdx.x < world) {
-    XrankSlot* dst = peers.p[threadIdx.x] + phase * KT_XRANK_MAX + rank;
+    XrankSlot* dst = to_peer + phase * KT_XRANK_MAX + rank;
     st_relaxed_sys_f64(&dst->value, local);
     st_release_sys_u64(&dst->epoch, epoch);
   }
   if (world > 1 && threadIdx.x < world) {
-    const XrankSlot* src = peers.p[rank] + phase * KT_XRANK_MAX + threadIdx.x;
+    const XrankSlot* src = own + phase * KT_XRANK_MAX + threadIdx.x;
     const unsigned long long t0 = gtimer_ns();
     bool ok = false;
     for (unsigned int it = 0; it < (1u << 26); ++it) {

@@ -38,7 +38,7 @@
 #define KT_SOFTMAX_CLUSTER 1  // > 1: every row split across a cluster of this many CTAs (rows_cluster.cuh)
 #endif
 #ifndef KT_SOFTMAX_STAGES
-#define KT_SOFTMAX_STAGES 3  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
+#define KT_SOFTMAX_STAGES 2  // rows in flight per CTA through the TMA bulk-copy ring (0: register kernel)
 #endif
 
 namespace kt {

@@ -96,6 +96,9 @@ class BenchmarkResult:
     library: str = ""
     problem: dict = field(default_factory=dict)
     gpu: Optional[int] = None
+    # mean_ms scaled to the work of the family's reference problem (a causal
+    # attention call does half the work of a non-causal one): what the tuner ranks by
+    normalized_ms: Optional[float] = None
 
     def to_dict(self) -> dict:
         """Serialise for JSON (raw_samples excluded, as in the reference)."""

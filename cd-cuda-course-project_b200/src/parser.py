@@ -271,7 +271,10 @@ def is_valid(kernel: str, params: dict) -> bool:
             if params.get("bk", 16) == 32 and not params.get("ffma_x2", 1):
                 return False
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
-        # the tcgen05 kernel ignores the FFMA axes
+        # the tcgen05 kernel ignores the FFMA axes; a stage holds a 128x32 A box and a BNx32 B box
+        # (48 KB at 128x256), so at most 4 stages of 128x256 fit the 227 KB of shared memory
+        if params.get("cta_tile", "128x128") == "128x256" and params.get("stages", 4) > 4:
+            return False
         return params.get("bk", 16) == 16 and params.get("ffma_x2", 1) == 1 and params.get("min_blocks", 2) == 2
     if fam == "attention":
         if params.get("kind", 1) == 2:

@@ -273,3 +273,16 @@ def test_shard_ranges_partition(n, world):
     assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         sharding.shard_range(n, world, world)
+
+
+def test_tuner_ranks_by_work_and_sizes_resources():
+    import autotune
+    d = {"B": 8, "H": 32, "S": 4096, "D": 128}
+    assert autotune.work_scale("attention", d, {"causal": True}) == pytest.approx(2.0, rel=1e-3)
+    assert autotune.work_scale("attention", d, {"causal": False}) == 1.0
+    assert autotune.work_scale("matmul", {"M": 8, "N": 8, "K": 8}, {"transpose_b": True}) == 1.0
+    # dynamic shared memory of the staged softmax (3 rows of 4096 floats) and the FA kernel
+    assert autotune.launch_resources("softmax", {"stages": 3}, {"cols": 4096})[0] == 3 * 4096 * 4 + 3 * 8 + 16
+    assert autotune.launch_resources("attention", {"kind": 1, "stages": 2, "v_stages": 2}, d) == (201984, 512)
+    assert autotune.kernel_function("attention", {"kind": 2, "causal": True})[1] == 512
+    assert autotune.kernel_function("softmax", {"cluster_size": 2})[0] == "rows_kernel"
