@@ -440,7 +440,39 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
     occ_rows = [r for r in results[:10] if r.occupancy is not None]
     if occ_rows:
         OccupancyAnalyzer.print_table(occ_rows, title=f"Occupancy — {kernel} top 10")
+    write_report(kernel, strategy_name, results, base_ms, dims or (results[0].problem if results else None),
+                 failures, conv, roof)
     return results
+
+
+def write_report(kernel: str, strategy_name: str, results: list[BenchmarkResult], base_ms: Optional[float],
+                 dims: Optional[dict], failures: list[dict], conv: ConvergenceLogger, roof: RooflineAnalyzer) -> None:
+    """results/{kernel}_report.md and the terminal summary (the reference's reporter.py)."""
+    from occupancy import parse_ptxas_stderr
+    from reporter import ReportGenerator, print_terminal_summary
+
+    def point(ms: float, causal: bool, variant: str) -> dict:
+        pt = roof.analyze(kernel, dims, ms, causal=causal, variant=variant)
+        return {"arithmetic_intensity": pt.arithmetic_intensity, "achieved_gflops": pt.achieved_gflops,
+                "achieved_gbps": pt.achieved_gbps, "bound_type": pt.bound_type, "efficiency_pct": pt.efficiency_pct,
+                "ceiling": pt.ceiling_name}
+
+    rg = ReportGenerator(kernel, strategy_name, results_dir())
+    rg.set_results(results, base_ms)
+    if results and dims:
+        b = results[0]
+        v = "ffma" if b.params.get("variant") == "ffma" else ""
+        rg.set_roofline_points(point(base_ms, False, v) if base_ms else None,
+                               point(b.mean_ms, bool(b.params.get("causal")), v))
+        rg.set_resource_report(parse_ptxas_stderr(b.ptx_info) or None)
+    n_failed = sum(1 for f in failures if str(f.get("error", "")).startswith("verification"))
+    n_ok = sum(1 for r in results if r.correctness_checked and r.is_correct)
+    rg.set_correctness(n_ok, n_failed)
+    conv_file = results_dir() / f"{kernel}_convergence.json"
+    if conv_file.exists():
+        rg.set_convergence(json.loads(conv_file.read_text()))
+    rg.generate()
+    print_terminal_summary(kernel, results, base_ms, strategy_name)
 
 
 def compile_only(kernels: list[str], strategy_name: str, budget: Optional[int], seed: int, workers: int) -> int:
@@ -517,6 +549,9 @@ def main(argv=None) -> int:
                                              a.matrix_size, a.budget, a.seed)
     finally:
         pool.close()
+    from reporter import print_final_summary
+    print_final_summary(all_results, {k: next((v["mean_ms"] for v in baselines.values() if v["kernel"] == k), None)
+                                      for k in kernels})
     print(f"[DONE] results in {results_dir()}")
     return 0 if all(all_results.values()) else 1
 

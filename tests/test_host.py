@@ -286,3 +286,53 @@ def test_tuner_ranks_by_work_and_sizes_resources():
     assert autotune.launch_resources("attention", {"kind": 1, "stages": 2, "v_stages": 2}, d) == (201984, 512)
     assert autotune.kernel_function("attention", {"kind": 2, "causal": True})[1] == 512
     assert autotune.kernel_function("softmax", {"cluster_size": 2})[0] == "rows_kernel"
+
+
+def test_report_generator_sections(tmp_path):
+    import reporter
+    from benchmark import BenchmarkResult
+    res = [BenchmarkResult(kernel="softmax", variant=f"v{i}", params={"block_size": 256, "stages": s},
+                           mean_ms=0.025 + 0.001 * i, ci_95_ms=0.0002, n_samples=10, speedup=200.0 - i,
+                           p_value=1e-30, is_significant=True, roofline_efficiency_pct=80.0 - i,
+                           occupancy=0.75, registers_per_thread=40, shared_mem_bytes=32784, normalized_ms=0.025,
+                           correctness_checked=True, is_correct=True, library="/x/softmax_v.so")
+           for i, s in enumerate((2, 3, 4))]
+    rg = reporter.ReportGenerator("softmax", "sha", tmp_path)
+    rg.set_results(res, baseline_ms=6.7)
+    rg.set_roofline_points({"arithmetic_intensity": 0.6, "achieved_gbps": 20.0, "achieved_gflops": 12.0,
+                            "bound_type": "memory", "efficiency_pct": 0.3, "ceiling": "HBM"},
+                           {"arithmetic_intensity": 0.6, "achieved_gbps": 5300.0, "achieved_gflops": 3300.0,
+                            "bound_type": "memory", "efficiency_pct": 81.0, "ceiling": "HBM"})
+    rg.set_correctness(3, 1)
+    rg.set_resource_report({"_ZN2kt6staged12softmax_rows": {"registers": 40, "smem_bytes": 256, "spill_stores": 0,
+                                                             "spill_loads": 0, "barriers": 1}})
+    rg.set_convergence({"kernel": "softmax", "n_evals": 15, "best_ms": 0.025, "curve": []})
+    path = rg.generate()
+    text = path.read_text()
+    assert path.name == "softmax_report.md"
+    for section in ("# Kernel auto-tuner report", "## Roofline", "## Top configurations", "## Occupancy",
+                    "## Resources of the best variant", "## Correctness", "## Convergence",
+                    "## Recommended configuration", "B200", "5300 GB/s", "stages"):
+        assert section in text, section
+    reporter.print_terminal_summary("softmax", res, 6.7, "sha")
+    reporter.print_final_summary({"softmax": res, "reduction": []}, {"softmax": 6.7})
+
+
+def test_tuned_layers_load_params_and_keep_weights(tmp_path):
+    import json as _json
+    import torch
+    import tuned_modules as tm
+    assert tm.load_best_params("layernorm", tmp_path) == {}
+    (tmp_path / "layernorm_tuning.json").write_text(_json.dumps(
+        {"best": {"params": {"stages": 2, "tma_box": 4096}, "library": str(tmp_path / "missing.so")}}))
+    assert tm.load_best_params("layernorm", tmp_path) == {"stages": 2, "tma_box": 4096}
+    assert tm.tuned_library("layernorm", tmp_path).path.name == "libkt.so"  # the tuned file is gone: default
+    model = torch.nn.Sequential(torch.nn.Linear(64, 32), torch.nn.LayerNorm(32), torch.nn.Linear(32, 8, bias=False))
+    w0 = model[0].weight.detach().clone()
+    tm.apply_tuned_layers(model, "all", results_dir=tmp_path)
+    assert isinstance(model[0], tm.TunedLinear) and isinstance(model[1], tm.TunedLayerNorm)
+    assert isinstance(model[2], tm.TunedLinear) and model[2].bias is None
+    assert torch.equal(model[0].weight, w0)
+    assert model[1].tuned_params == {"stages": 2, "tma_box": 4096}
+    with pytest.raises(ValueError):
+        tm.TunedMultiheadAttention(96, 3)  # head dim 32 is not built
