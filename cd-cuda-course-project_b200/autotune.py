@@ -123,8 +123,8 @@ def kernel_function(kernel: str, p: dict) -> tuple[str, int]:
         if p.get("kind", 1) == 2:
             # loaders, MMA lane, 2 x 4 softmax warps, 4 epilogue warps
             return f"fa2_fwd_kernelILi128ELi4ELi4ELb{c}", 512
-        # 3 loader/MMA warps + 8 softmax warps + 4 epilogue warps
-        return f"fa_fwd_kernelILi128ELi{int(p.get('stages', 2))}ELb{c}", 480
+        # 3 loader/MMA warps + 8 softmax warps + 4 epilogue warps (+ 1 P·V-issuing warp with two issuers)
+        return f"fa_fwd_kernelILi128ELi{int(p.get('stages', 2))}ELb{c}", 512 if int(p.get("issuers", 2)) == 2 else 480
     raise ValueError(f"unknown kernel {kernel!r}")
 
 

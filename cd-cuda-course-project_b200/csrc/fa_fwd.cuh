@@ -32,6 +32,7 @@
 // Every mbarrier wait is bounded; a timeout records DEV_MBAR_TIMEOUT and the
 // CTA unwinds (loader drains its copies, MMAs drain before TMEM is released).
 #pragma once
+#include <type_traits>
 #include "kt_common.cuh"
 #include "sm100.cuh"
 #include "fa_fwd2.cuh"
@@ -48,6 +49,16 @@
 #ifndef KT_FA_EXP16
 #define KT_FA_EXP16 0  // 1: exponentials as packed half-precision pairs (ex2.approx.f16x2: two results per MUFU op)
 #endif
+#ifndef KT_FA_ISSUERS
+#define KT_FA_ISSUERS 2  // 2: S = Q·K^T and O += P·V issued by two warps (one thread issues tcgen05.mma at ~73 clocks
+                         // per instruction, above the 64-clock 128x128x16 MMA); 1: one issuing thread
+#endif
+#ifndef KT_FA_SPEC
+#define KT_FA_SPEC 1  // 1: exponentials start with the running max before the partner's half max is read
+#endif
+#ifndef KT_FA_RELOAD
+#define KT_FA_RELOAD 0  // 1: the exponential pass reloads the scores from TMEM 32 columns at a time
+#endif
 #ifndef KT_FA_POLY
 #define KT_FA_POLY 0  // 1: every 4th value pair of exponentials on the FMA pipe (measured slower: the FMA/ALU
                       // pipes, not MUFU, limit the softmax warps)
@@ -61,7 +72,8 @@ constexpr int BN = 128;  // keys per tile (the S accumulator is 128 columns)
 constexpr int SOFTMAX_WARPS = 8;
 constexpr int V_LOADER_WARP = 2 + SOFTMAX_WARPS;
 constexpr int EPI_THREADS = 128;  // warps 11-14: one query row per thread
-constexpr int THREADS = 96 + 32 * SOFTMAX_WARPS + EPI_THREADS;
+constexpr int PV_WARP = V_LOADER_WARP + 1 + EPI_THREADS / 32;  // warp 15 (two issuers): issues O += P·V
+constexpr int THREADS = 96 + 32 * SOFTMAX_WARPS + EPI_THREADS + (KT_FA_ISSUERS == 2 ? 32 : 0);
 constexpr int SOFTMAX_THREADS = 32 * SOFTMAX_WARPS;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only when the max grows by > 2^8
 constexpr int kHeadGroup = 8;              // causal scheduling: heads whose K/V share L2
@@ -81,8 +93,8 @@ struct Cfg {
   static constexpr int RED_OFFSET = V_OFFSET + VSTAGES * V_BYTES;
   static constexpr int BAR_OFFSET = RED_OFFSET + 8 * 128 * 4;
   // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[2], s_free[2],
-  // p_full[2], l_full[2], l_empty[2], o_done, o_final, o_empty, done, pair[4]
-  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 10 + 4 + 4;
+  // p_full[2], l_full[2], l_empty[2], o_done, o_final, o_empty, done, pair[4], o_done_odd
+  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 10 + 4 + 4 + 1;
   static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
@@ -186,7 +198,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   auto p_full = [&](int b) { return bar0 + 8u * (R + 4 + b); };
   auto l_full = [&](int b) { return bar0 + 8u * (R + 6 + b); };
   auto l_empty = [&](int b) { return bar0 + 8u * (R + 8 + b); };
-  const uint32_t o_done = bar0 + 8u * (R + 10);   // one phase per P·V product
+  const uint32_t o_done = bar0 + 8u * (R + 10);   // one phase per P·V product (two issuers: even tiles only)
+  // two issuers: o_done_of(t) completes once per P_t·V of tile parity t&1
+  auto o_done_of = [&](int t) { return (t & 1) ? bar0 + 8u * (R + 18) : o_done; };
   const uint32_t o_final = bar0 + 8u * (R + 11);  // one phase per item: its last P·V product landed
   const uint32_t o_empty = bar0 + 8u * (R + 12);  // one phase per item: the epilogue has read O
   const uint32_t done_bar = bar0 + 8u * (R + 13);
@@ -218,9 +232,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       mbar_init(v_empty(s), 1);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_done_of(1), 1);
     mbar_init(o_final, 1);
     mbar_init(o_empty, EPI_THREADS);
-    mbar_init(done_bar, 1);
+    mbar_init(done_bar, KT_FA_ISSUERS);
     for (int q = 0; q < 4; ++q) mbar_init(pair_bar0 + 8u * q, 64);
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -299,8 +314,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           if (pending[i]) (void)mbar_wait(is_k ? k_full(i) : v_full(i), last_ph[i]);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || (KT_FA_ISSUERS == 2 && warp == PV_WARP)) {
     if (lane == 0) {
+      const bool s_issuer = (warp == 1), pv_issuer = (KT_FA_ISSUERS == 1 || warp == PV_WARP);
       constexpr uint32_t idesc_s = idesc_f32acc(kFmtBF16, BM, BN, 0, 0);
       constexpr uint32_t idesc_o = idesc_f32acc(kFmtBF16, BM, D, 0, 1);
       int kc = 0, vc = 0;  // K / V ring positions
@@ -341,12 +357,46 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           mma_f16_ts_w(o_tmem, p_tmem + (uint32_t)(kk * 8), v_lo + (uint32_t)(kk * 16 * 128 / 16), v_hi, idesc_o,
                        (!first || kk > 0) ? 1u : 0u);
         }
-        mma_commit(o_done);
+        mma_commit(KT_FA_ISSUERS == 2 ? o_done_of(t) : o_done);
         mma_commit(v_empty(vc % VSTAGES));
         if (last) mma_commit(o_final);
         ++vc;
         return true;
       };
+      // Two issuers: warp 1 issues S_t as soon as its K tile and S buffer are free
+      // and P_{t-2}·V is complete (then the softmax's parity waits on o_done_of
+      // are exact: at tile t at most P_{t-1}·V is outstanding); warp PV_WARP
+      // issues P_t·V as soon as P_t is in TMEM. One issuer: the order below.
+      if (KT_FA_ISSUERS == 2) {
+        int t = 0, k = 0;
+        for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
+          int qt, bh;
+          item_coords<CAUSAL>(w, num_q_tiles, BH, qt, bh);
+          const int n_kv = kv_tiles<CAUSAL>(qt, S);
+          if (s_issuer && !mbar_wait(q_full(k & 1), (uint32_t)(k >> 1) & 1u)) {
+            timed_out = true;
+            break;
+          }
+          for (int j = 0; j < n_kv; ++j, ++t) {
+            if (s_issuer) {
+              if (!mbar_wait(k_full(kc % STAGES), (uint32_t)(kc / STAGES) & 1u) ||
+                  !mbar_wait(s_free(t & 1), ((uint32_t)(t >> 1) & 1u) ^ 1u) ||
+                  (t >= 2 && !mbar_wait(o_done_of(t - 2), (uint32_t)((t - 2) >> 1) & 1u))) {
+                timed_out = true;
+                break;
+              }
+              tc_fence_after();
+              issue_s(t, k & 1);
+              if (j == n_kv - 1) mma_commit(q_empty(k & 1));
+            }
+            if (pv_issuer && !s_issuer && !pv_step(t, k, j == 0, j == n_kv - 1)) {
+              timed_out = true;
+              break;
+            }
+          }
+        }
+        mma_commit(done_bar);
+      } else {
       // Issue order S_t, P_{t-1}·V: the tensor core computes the next scores while
       // the softmax warps work on the current ones, across item boundaries too.
       int t = 0, k = 0;
@@ -382,6 +432,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       }
       if (!timed_out && have_prev && !pv_step(t - 1, prev_k, prev_first, prev_last)) timed_out = true;
       mma_commit(done_bar);
+      }
+      (void)s_issuer;
+      (void)pv_issuer;
     }
   } else if (warp < V_LOADER_WARP) {
     // softmax: TMEM lane quarter = warp % 4, the two warps of a quarter split the columns
@@ -425,77 +478,128 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < HC; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sv[c]));
-        // exchange the half-row maxima (slots double-buffered by tile parity: the
-        // partner may still read the previous tile's slot while this thread writes)
+        const float mh = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        // publish the half-row maximum to the partner warp (slots double-buffered by
+        // tile parity: the partner may still read the previous tile's slot)
         float* red_max = red + (b * 2) * 128;
-        red_max[half * 128 + row] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        red_max[half * 128 + row] = mh;
         mbar_arrive(pair_mbar);  // release: the write above is visible to the partner after its wait
-        if (!__all_sync(0xffffffffu, mbar_wait(pair_mbar, (uint32_t)t & 1u))) {
-          timed_out = true;
-          break;
-        }
-        const float mx = fmaxf(red_max[row], red_max[128 + row]);
-        const float m_tile = mx * scale_log2;
-        const bool raise = m_tile > m_run + kRescaleThreshold;
-        float alpha = 1.f;
-        if (raise) {
-          alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_tile);
-          m_run = m_tile;
-          l_part *= alpha;
-        }
-        // O holds P_0..P_{j-1}·V of this item: rescale this half of it once the
-        // previous P·V product has landed. o_done has completed t-1 or t phases
-        // here (s_full of tile t was committed after P_{t-2}·V was issued, and
-        // P_t·V needs this thread's P_t), so a parity wait is exact.
-        if (j > 0 && __any_sync(0xffffffffu, raise)) {
-          if (!__all_sync(0xffffffffu, mbar_wait(o_done, (uint32_t)(t - 1) & 1u))) {
+        const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2));
+        // p = 2^(s·c − m) (masked entries are −inf -> 0) into TMEM as bf16; returns this half's sum.
+        // The polynomial share is chosen per tile (masked tiles use MUFU only).
+        auto make_p = [&](float m, auto poly_tag) -> float {
+          constexpr bool POLY = decltype(poly_tag)::value;
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int c = 0; c < HC; c += 32) {
+            uint32_t pk[16];
+            uint32_t sc[32];
+            if (KT_FA_RELOAD) {
+              // scores again from TMEM, 32 columns at a time: only this chunk is live
+              tmem_ld32(s_addr + (uint32_t)c, sc);
+              tmem_ld_wait();
+              if (mask_tile) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const int key = key0 + c + i;
+                  if (!(key < S && (!CAUSAL || key <= qrow))) sc[i] = __float_as_uint(-INFINITY);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) sc[i] = sv[c + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float x0 = fmaf(__uint_as_float(sc[2 * i]), scale_log2, -m);
+              const float x1 = fmaf(__uint_as_float(sc[2 * i + 1]), scale_log2, -m);
+              float p0, p1;
+              if (KT_FA_EXP16) {
+                ex2_h2(x0, x1, p0, p1);
+              } else if (POLY && (i & 3) == 3) {
+                p0 = ex2_poly(x0);
+                p1 = ex2_poly(x1);
+              } else {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              }
+              s4[i & 3] += p0 + p1;
+              pk[i] = pack_bf16(p0, p1);
+            }
+            tmem_st16(p_addr + (uint32_t)(c / 2), pk);
+          }
+          return (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        };
+        auto p_sum = [&](float m) -> float {
+          if (KT_FA_POLY && !mask_tile) return make_p(m, std::true_type{});
+          return make_p(m, std::false_type{});
+        };
+        // Speculation (j > 0): when no lane of this warp needs its running max raised
+        // by its own half, P is computed with the current running max before the
+        // partner's half maximum is read, so the exchange overlaps the exponentials.
+        // Only if the partner's half then asks for a raise are P and the sum redone
+        // below with the new maximum (the MMA reads P only after p_full).
+        bool pair_seen = false, finished = false;
+        if (KT_FA_SPEC && j > 0 && !__any_sync(0xffffffffu, mh * scale_log2 > m_run + kRescaleThreshold)) {
+          const float spec_sum = p_sum(m_run);
+          if (!__all_sync(0xffffffffu, mbar_wait(pair_mbar, (uint32_t)t & 1u))) {
             timed_out = true;
             break;
           }
-          tc_fence_after();
+          pair_seen = true;
+          const float mx_s = fmaxf(red_max[row], red_max[128 + row]);
+          if (!__any_sync(0xffffffffu, mx_s * scale_log2 > m_run + kRescaleThreshold)) {
+            l_part += spec_sum;
+            finished = true;
+          } else {
+            tmem_st_wait();  // the speculative P is rewritten below
+          }
+        }
+        if (!finished) {
+          if (!pair_seen && !__all_sync(0xffffffffu, mbar_wait(pair_mbar, (uint32_t)t & 1u))) {
+            timed_out = true;
+            break;
+          }
+          const float mx = fmaxf(red_max[row], red_max[128 + row]);
+          const float m_tile = mx * scale_log2;
+          const bool raise = m_tile > m_run + kRescaleThreshold;
+          float alpha = 1.f;
+          if (raise) {
+            alpha = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_tile);
+            m_run = m_tile;
+            l_part *= alpha;
+          }
+          // O holds P_0..P_{j-1}·V of this item: rescale this half of it once the
+          // previous P·V product has landed. o_done has completed t-1 or t phases
+          // here (s_full of tile t was committed after P_{t-2}·V was issued, and
+          // P_t·V needs this thread's P_t), so a parity wait is exact.
+          if (j > 0 && __any_sync(0xffffffffu, raise)) {
+            const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), (uint32_t)((t - 1) >> 1) & 1u)
+                                                    : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
+            if (!__all_sync(0xffffffffu, o_ready)) {
+              timed_out = true;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < HD; c += 32) {
-            uint32_t v[32];
-            const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)(half * HD + c);
-            tmem_ld32(oa, v);
-            tmem_ld_wait();
-            uint32_t w0[16], w1[16];
+            for (int c = 0; c < HD; c += 32) {
+              uint32_t v[32];
+              const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)(half * HD + c);
+              tmem_ld32(oa, v);
+              tmem_ld_wait();
+              uint32_t w0[16], w1[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              w0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-              w1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
+              for (int i = 0; i < 16; ++i) {
+                w0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+                w1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
+              }
+              tmem_st16(oa, w0);
+              tmem_st16(oa + 16u, w1);
             }
-            tmem_st16(oa, w0);
-            tmem_st16(oa + 16u, w1);
+            tmem_st_wait();
           }
-          tmem_st_wait();
+          l_part += p_sum(m_run);
         }
-        // p = 2^(s·c − m) (masked entries are −inf -> 0), partial sum, bf16 P into TMEM
-        const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2));
-        float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < HC; c += 32) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float x0 = fmaf(__uint_as_float(sv[c + 2 * i]), scale_log2, -m_run);
-            const float x1 = fmaf(__uint_as_float(sv[c + 2 * i + 1]), scale_log2, -m_run);
-            float p0, p1;
-            if (KT_FA_EXP16) {
-              ex2_h2(x0, x1, p0, p1);
-            } else if (KT_FA_POLY && !mask_tile && (i & 3) == 3) {
-              p0 = ex2_poly(x0);
-              p1 = ex2_poly(x1);
-            } else {
-              p0 = ex2(x0);
-              p1 = ex2(x1);
-            }
-            s4[i & 3] += p0 + p1;
-            pk[i] = pack_bf16(p0, p1);
-          }
-          tmem_st16(p_addr + (uint32_t)(c / 2), pk);
-        }
-        l_part += (s4[0] + s4[1]) + (s4[2] + s4[3]);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(s_free(b));

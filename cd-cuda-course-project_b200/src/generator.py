@@ -59,7 +59,8 @@ MACROS: dict[str, dict[str, str]] = {
     "matmul": {"bk": "KT_FFMA_BK", "ffma_x2": "KT_FFMA_X2", "min_blocks": "KT_FFMA_MINB",
                "cta_tile": "KT_TC_BN", "stages": "KT_TC_STAGES"},
     "attention": {"kind": "KT_FA_KIND", "stages": "KT_FA_STAGES", "v_stages": "KT_FA_VSTAGES",
-                  "poly_exp2": "KT_FA_POLY", "order": "KT_FA2_ORDER", "poly_every": "KT_FA2_POLY", "exp16": "KT_FA_EXP16"},
+                  "poly_exp2": "KT_FA_POLY", "order": "KT_FA2_ORDER", "poly_every": "KT_FA2_POLY", "exp16": "KT_FA_EXP16",
+                  "spec": "KT_FA_SPEC", "reload": "KT_FA_RELOAD", "issuers": "KT_FA_ISSUERS"},
 }
 ONLY = {"softmax": "KT_ONLY_SOFTMAX", "layernorm": "KT_ONLY_LAYERNORM", "reduction": "KT_ONLY_REDUCE",
         "matmul": "KT_ONLY_GEMM", "attention": "KT_ONLY_FA"}

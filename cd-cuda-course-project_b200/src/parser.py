@@ -228,6 +228,7 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["stages"] = [1, 2, 3]       # kind 1: K ring depth
         space["v_stages"] = [1, 2, 3]     # kind 1: V ring depth
         space["poly_exp2"] = [0, 1]       # kind 1: every 4th exponential pair on the FMA pipe
+        space["issuers"] = [1, 2]         # kind 1: threads issuing tcgen05.mma (2: S and P·V from two warps)
         space["order"] = [0, 1]           # kind 2: MMA issue order (0 ping-pong, 1 in phase)
         space["poly_every"] = [0, 4, 8]   # kind 2: every n-th exponential pair on the FMA pipe (0: none)
         space["causal"] = [False, True]
@@ -279,7 +280,8 @@ def is_valid(kernel: str, params: dict) -> bool:
     if fam == "attention":
         if params.get("kind", 1) == 2:
             # the kind-1 axes do not shape this kernel: one representative point
-            return (params.get("stages", 2), params.get("v_stages", 2), params.get("poly_exp2", 0)) == (2, 2, 0)
+            return (params.get("stages", 2), params.get("v_stages", 2), params.get("poly_exp2", 0),
+                    params.get("issuers", 2)) == (2, 2, 0, 2)
         if params.get("order", 0) != 0 or params.get("poly_every", 0) != 0:
             return False
         # head dim 128: two Q buffers + (K + V slots) x 32 KB must fit the 227 KB of shared memory
