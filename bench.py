@@ -89,8 +89,8 @@ KERNEL_ID = {
     "layernorm": "layernorm_rows<256,4,2>",
     "matmul_tf32": "gemm_tf32_kernel<256,4,0>",
     "matmul_tf32_tb": "gemm_tf32_kernel<256,4,1>",
-    "matmul_ffma": "sgemm_128x128<0,1,16,2>",
-    "matmul_ffma_tb": "sgemm_128x128<1,1,16,2>",
+    "matmul_ffma": "sgemm_128x256<0,1,8>",
+    "matmul_ffma_tb": "sgemm_128x256<1,1,8>",
     "attention": "fa_fwd_kernel<128,2,0>",
     "attention_causal": "fa_fwd_kernel<128,2,1>",
 }

@@ -116,7 +116,9 @@ def kernel_function(kernel: str, p: dict) -> tuple[str, int]:
     if kernel == "reduction":
         return "sum_f32", int(p.get("block_size", 512))
     if kernel == "matmul":
-        return ("sgemm_128x128", 256) if p.get("variant") == "ffma" else ("gemm_tf32_kernel", 192)
+        if p.get("variant") == "ffma":
+            return ("sgemm_128x256" if int(p.get("ffma_wide", 1)) else "sgemm_128x128"), 256
+        return "gemm_tf32_kernel", 192
     if kernel == "attention":
         # the library holds D=64 and D=128 instances; the tuned size has D=128
         c = int(bool(p.get("causal")))

@@ -18,6 +18,9 @@
 #ifndef KT_FFMA_MINB
 #define KT_FFMA_MINB 2
 #endif
+#ifndef KT_FFMA_WIDE
+#define KT_FFMA_WIDE 1  // 1: 128x256 CTA tile, 8x16 outputs per thread (sgemm_128x256); 0: 128x128, 8x8
+#endif
 #ifndef KT_FFMA_X2
 #define KT_FFMA_X2 0  // 0: scalar FFMA (sgemm_128x128); 1: packed fma.rn.f32x2 kernel (sgemm_x2_128x128), measured slower
 #endif
@@ -147,6 +150,135 @@ sgemm_128x128(const float* __restrict__ A, const float* __restrict__ B, float* _
       const int64_t col = n0 + h * 64 + tx * 4;
       float* c = C + row * N + col;
       const float4 v = make_float4(acc[i][h * 4 + 0], acc[i][h * 4 + 1], acc[i][h * 4 + 2], acc[i][h * 4 + 3]);
+      if (VEC && col + 3 < N) {
+        *reinterpret_cast<float4*>(c) = v;
+      } else {
+        if (col + 0 < N) c[0] = v.x;
+        if (col + 1 < N) c[1] = v.y;
+        if (col + 2 < N) c[2] = v.z;
+        if (col + 3 < N) c[3] = v.w;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Wide variant: a 128x256 CTA tile, 256 threads, 8x16 outputs per thread
+// (rows ty*4+{0..3} and 64+ty*4+{0..3}, columns tx*4+{0..3} + {0, 64, 128, 192}).
+// Every k step is 128 FMAs for six 128-bit shared loads (64 for four in the
+// 128x128 kernel): a larger share of the issue slots goes to the FMA pipe. One
+// CTA per SM (about 170 registers per thread); k-major shared tiles
+// double-buffered through registers, as in sgemm_128x128. Results are
+// bit-identical to sgemm_128x128 (one fp32 fma per k, k ascending).
+// ---------------------------------------------------------------------------
+constexpr int WBN = 256;
+
+template <bool TB, bool VEC, int BK>
+__global__ void __launch_bounds__(THREADS, 1)
+sgemm_128x256(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int64_t M, int64_t N,
+              int64_t K) {
+  static_assert(BK == 8 || BK == 16, "BK");
+  __shared__ __align__(16) float As[2][BK][BM + PAD];
+  __shared__ __align__(16) float Bs[2][BK][WBN + PAD];
+  constexpr int AV = BM * BK / 4 / THREADS;
+  constexpr int BV = WBN * BK / 4 / THREADS;
+  static_assert(AV >= 1 && BV >= 1, "tile/threads");
+  constexpr int KQ = BK / 4;
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * WBN;
+
+  float4 ra[AV], rb[BV];
+  auto load_tile = [&](int64_t k0) {
+#pragma unroll
+    for (int i = 0; i < AV; ++i) {
+      const int e = tid + i * THREADS;
+      const int r = e / KQ, kq = (e % KQ) * 4;
+      ra[i] = load4<VEC>(A, m0 + r, k0 + kq, M, K, K);
+    }
+#pragma unroll
+    for (int i = 0; i < BV; ++i) {
+      const int e = tid + i * THREADS;
+      if (TB) {
+        const int r = e / KQ, kq = (e % KQ) * 4;
+        rb[i] = load4<VEC>(B, n0 + r, k0 + kq, N, K, K);
+      } else {
+        const int kr = e / (WBN / 4), nq = (e % (WBN / 4)) * 4;
+        rb[i] = load4<VEC>(B, k0 + kr, n0 + nq, K, N, N);
+      }
+    }
+  };
+  auto store_tile = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < AV; ++i) {
+      const int e = tid + i * THREADS;
+      const int r = e / KQ, kq = (e % KQ) * 4;
+      As[buf][kq + 0][r] = ra[i].x;
+      As[buf][kq + 1][r] = ra[i].y;
+      As[buf][kq + 2][r] = ra[i].z;
+      As[buf][kq + 3][r] = ra[i].w;
+    }
+#pragma unroll
+    for (int i = 0; i < BV; ++i) {
+      const int e = tid + i * THREADS;
+      if (TB) {
+        const int r = e / KQ, kq = (e % KQ) * 4;
+        Bs[buf][kq + 0][r] = rb[i].x;
+        Bs[buf][kq + 1][r] = rb[i].y;
+        Bs[buf][kq + 2][r] = rb[i].z;
+        Bs[buf][kq + 3][r] = rb[i].w;
+      } else {
+        const int kr = e / (WBN / 4), nq = (e % (WBN / 4)) * 4;
+        *reinterpret_cast<float4*>(&Bs[buf][kr][nq]) = rb[i];
+      }
+    }
+  };
+
+  float acc[8][16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[i][j] = 0.f;
+
+  const int64_t nk = (K + BK - 1) / BK;
+  load_tile(0);
+  store_tile(0);
+  __syncthreads();
+  for (int64_t t = 0; t < nk; ++t) {
+    const int cur = (int)(t & 1);
+    if (t + 1 < nk) load_tile((t + 1) * BK);
+#pragma unroll
+    for (int k = 0; k < BK; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][k][ty * 4 + 64]);
+      float b[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 bq = *reinterpret_cast<const float4*>(&Bs[cur][k][tx * 4 + 64 * q]);
+        b[4 * q + 0] = bq.x;
+        b[4 * q + 1] = bq.y;
+        b[4 * q + 2] = bq.z;
+        b[4 * q + 3] = bq.w;
+      }
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    if (t + 1 < nk) store_tile(cur ^ 1);
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (row >= M) continue;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int64_t col = n0 + q * 64 + tx * 4;
+      float* c = C + row * N + col;
+      const float4 v = make_float4(acc[i][4 * q + 0], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]);
       if (VEC && col + 3 < N) {
         *reinterpret_cast<float4*>(c) = v;
       } else {
@@ -310,7 +442,10 @@ sgemm_x2_128x128(const float* __restrict__ A, const float* __restrict__ B, float
 template <bool TB, bool VEC>
 inline int launch_t(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  if constexpr (KT_FFMA_X2 != 0) {
+  if constexpr (KT_FFMA_WIDE != 0) {
+    dim3 wgrid((unsigned)((N + WBN - 1) / WBN), (unsigned)((M + BM - 1) / BM));
+    sgemm_128x256<TB, VEC, 8><<<wgrid, THREADS, 0, st>>>(A, B, C, M, N, K);  // 8-deep k tiles: 24.5 KB static smem
+  } else if constexpr (KT_FFMA_X2 != 0) {
     auto kern = sgemm_x2_128x128<TB, VEC, KT_FFMA_BK, KT_FFMA_MINB>;
     constexpr size_t smem = X2Smem<KT_FFMA_BK>::BYTES;
     int rc = ensure_smem((const void*)kern, smem, "gemm ffma: smem attribute");

@@ -56,7 +56,7 @@ MACROS: dict[str, dict[str, str]] = {
     "layernorm": {"block_size": "KT_LN_BLOCK", "vec_per_thread": "KT_LN_VPT", "min_blocks": "KT_LN_MINB",
                   "stages": "KT_LN_STAGES", "cluster_size": "KT_LN_CLUSTER", "tma_box": "KT_ROWS_BOX"},
     "reduction": {"block_size": "KT_REDUCE_BLOCK", "unroll": "KT_REDUCE_UNROLL", "blocks_per_sm": "KT_REDUCE_BPSM"},
-    "matmul": {"bk": "KT_FFMA_BK", "ffma_x2": "KT_FFMA_X2", "min_blocks": "KT_FFMA_MINB",
+    "matmul": {"bk": "KT_FFMA_BK", "ffma_x2": "KT_FFMA_X2", "ffma_wide": "KT_FFMA_WIDE", "min_blocks": "KT_FFMA_MINB",
                "cta_tile": "KT_TC_BN", "stages": "KT_TC_STAGES"},
     "attention": {"kind": "KT_FA_KIND", "stages": "KT_FA_STAGES", "v_stages": "KT_FA_VSTAGES",
                   "poly_exp2": "KT_FA_POLY", "order": "KT_FA2_ORDER", "poly_every": "KT_FA2_POLY", "exp16": "KT_FA_EXP16",

@@ -220,6 +220,7 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["transpose_b"] = [False, True]
         space["bk"] = [8, 16, 32]
         space["ffma_x2"] = [0, 1]         # ffma: packed fma.rn.f32x2 (two fp32 FMAs per lane per instruction)
+        space["ffma_wide"] = [0, 1]       # ffma: 128x256 CTA tile, 8x16 outputs per thread (k tile 8)
         space["min_blocks"] = [1, 2]      # ffma: resident CTAs per SM asked of the register allocator
         space["cta_tile"] = ["128x128", "128x256"]
         space["stages"] = [3, 4, 5, 6]
@@ -271,12 +272,17 @@ def is_valid(kernel: str, params: dict) -> bool:
             # kernel's static shared tiles exceed 48 KB at bk=32
             if params.get("bk", 16) == 32 and not params.get("ffma_x2", 1):
                 return False
+            if params.get("ffma_wide", 0):
+                # the wide kernel has its own fixed shape: one representative point
+                if params.get("ffma_x2", 0) or params.get("bk", 8) != 8 or params.get("min_blocks", 1) != 1:
+                    return False
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
         # the tcgen05 kernel ignores the FFMA axes; a stage holds a 128x32 A box and a BNx32 B box
         # (48 KB at 128x256), so at most 4 stages of 128x256 fit the 227 KB of shared memory
         if params.get("cta_tile", "128x128") == "128x256" and params.get("stages", 4) > 4:
             return False
-        return params.get("bk", 16) == 16 and params.get("ffma_x2", 1) == 1 and params.get("min_blocks", 2) == 2
+        return params.get("bk", 16) == 16 and params.get("ffma_x2", 1) == 1 and params.get("min_blocks", 2) == 2 \
+            and params.get("ffma_wide", 0) == 0
     if fam == "attention":
         if params.get("kind", 1) == 2:
             # the kind-1 axes do not shape this kernel: one representative point
