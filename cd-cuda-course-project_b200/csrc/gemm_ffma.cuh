@@ -12,6 +12,13 @@
 #pragma once
 #include "kt_common.cuh"
 
+// k tile of the wide kernel: the tuner's bk when a variant sets it, else 8 (measured
+// 51.2 against 48.5 TFLOP/s with 16 at 8192^3)
+#ifdef KT_FFMA_BK
+#define KT_FFMA_WIDE_BK (KT_FFMA_BK >= 16 ? 16 : 8)
+#else
+#define KT_FFMA_WIDE_BK 8
+#endif
 #ifndef KT_FFMA_BK
 #define KT_FFMA_BK 16
 #endif
@@ -173,13 +180,20 @@ sgemm_128x128(const float* __restrict__ A, const float* __restrict__ B, float* _
 // ---------------------------------------------------------------------------
 constexpr int WBN = 256;
 
+template <int BK>
+constexpr size_t wide_smem_bytes() {
+  return sizeof(float) * 2 * (size_t)BK * ((BM + PAD) + (WBN + PAD));
+}
+
 template <bool TB, bool VEC, int BK>
 __global__ void __launch_bounds__(THREADS, 1)
 sgemm_128x256(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int64_t M, int64_t N,
               int64_t K) {
   static_assert(BK == 8 || BK == 16, "BK");
-  __shared__ __align__(16) float As[2][BK][BM + PAD];
-  __shared__ __align__(16) float Bs[2][BK][WBN + PAD];
+  // dynamic shared memory: [2][BK][BM + PAD] A tiles, then [2][BK][WBN + PAD] B tiles
+  extern __shared__ __align__(16) float wide_smem[];
+  auto As = reinterpret_cast<float(*)[BK][BM + PAD]>(wide_smem);
+  auto Bs = reinterpret_cast<float(*)[BK][WBN + PAD]>(wide_smem + 2 * BK * (BM + PAD));
   constexpr int AV = BM * BK / 4 / THREADS;
   constexpr int BV = WBN * BK / 4 / THREADS;
   static_assert(AV >= 1 && BV >= 1, "tile/threads");
@@ -444,7 +458,12 @@ inline int launch_t(const float* A, const float* B, float* C, int64_t M, int64_t
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
   if constexpr (KT_FFMA_WIDE != 0) {
     dim3 wgrid((unsigned)((N + WBN - 1) / WBN), (unsigned)((M + BM - 1) / BM));
-    sgemm_128x256<TB, VEC, 8><<<wgrid, THREADS, 0, st>>>(A, B, C, M, N, K);  // 8-deep k tiles: 24.5 KB static smem
+    constexpr int WBK = KT_FFMA_WIDE_BK;
+    auto kern = sgemm_128x256<TB, VEC, WBK>;
+    constexpr size_t smem = wide_smem_bytes<WBK>();
+    int rc = ensure_smem((const void*)kern, smem, "gemm ffma: smem attribute");
+    if (rc != KT_OK) return rc;
+    kern<<<wgrid, THREADS, smem, st>>>(A, B, C, M, N, K);
   } else if constexpr (KT_FFMA_X2 != 0) {
     auto kern = sgemm_x2_128x128<TB, VEC, KT_FFMA_BK, KT_FFMA_MINB>;
     constexpr size_t smem = X2Smem<KT_FFMA_BK>::BYTES;

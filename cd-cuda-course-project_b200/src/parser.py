@@ -220,7 +220,7 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["transpose_b"] = [False, True]
         space["bk"] = [8, 16, 32]
         space["ffma_x2"] = [0, 1]         # ffma: packed fma.rn.f32x2 (two fp32 FMAs per lane per instruction)
-        space["ffma_wide"] = [0, 1]       # ffma: 128x256 CTA tile, 8x16 outputs per thread (k tile 8)
+        space["ffma_wide"] = [0, 1]       # ffma: 128x256 CTA tile, 8x16 outputs per thread (k tile 8 or 16)
         space["min_blocks"] = [1, 2]      # ffma: resident CTAs per SM asked of the register allocator
         space["cta_tile"] = ["128x128", "128x256"]
         space["stages"] = [3, 4, 5, 6]
@@ -274,7 +274,7 @@ def is_valid(kernel: str, params: dict) -> bool:
                 return False
             if params.get("ffma_wide", 0):
                 # the wide kernel has its own fixed shape: one representative point
-                if params.get("ffma_x2", 0) or params.get("bk", 8) != 8 or params.get("min_blocks", 1) != 1:
+                if params.get("ffma_x2", 0) or params.get("bk", 8) not in (8, 16) or params.get("min_blocks", 1) != 1:
                     return False
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
         # the tcgen05 kernel ignores the FFMA axes; a stage holds a 128x32 A box and a BNx32 B box
