@@ -53,6 +53,15 @@
 #define KT_FA_ISSUERS 2  // 2: S = Q·K^T and O += P·V issued by two warps (one thread issues tcgen05.mma at ~73 clocks
                          // per instruction, above the 64-clock 128x128x16 MMA); 1: one issuing thread
 #endif
+#ifndef KT_FA_ALT
+#define KT_FA_ALT 0  // 1: the two softmax warps of a TMEM lane quarter take alternate S tiles, whole 128-key rows
+#endif
+#ifndef KT_FA_SBUF
+#define KT_FA_SBUF 2  // S accumulators in TMEM: 2 (P in its own columns) or 3 (P written over its S tile)
+#endif
+#ifndef KT_FA_X2
+#define KT_FA_X2 0  // 1: the exponent arguments and row sums in packed fma.rn.f32x2 / add.rn.f32x2
+#endif
 #ifndef KT_FA_SPEC
 #define KT_FA_SPEC 1  // 1: exponentials start with the running max before the partner's half max is read
 #endif
@@ -89,16 +98,22 @@ struct Cfg {
   static constexpr int Q_OFFSET = 0;                // two Q buffers: the next item's tile loads early
   static constexpr int K_OFFSET = 2 * Q_BYTES;
   static constexpr int V_OFFSET = K_OFFSET + STAGES * K_BYTES;
-  // [2 tile parity][2 half][128 rows] softmax maxima + [2 item parity][2 half][128 rows] row sums
+  // column halves: [2 tile parity][2 half][128 rows] softmax maxima + [2 item parity][2 half][128 rows] row sums;
+  // alternate tiles: [2 item parity][128] running max, [2 item parity][2 parity][128] row-sum shares and
+  // [2 item parity][2 parity][128] the maxima they are relative to
   static constexpr int RED_OFFSET = V_OFFSET + VSTAGES * V_BYTES;
-  static constexpr int BAR_OFFSET = RED_OFFSET + 8 * 128 * 4;
-  // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[2], s_free[2],
-  // p_full[2], l_full[2], l_empty[2], o_done, o_final, o_empty, done, pair[4], o_done_odd
-  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 10 + 4 + 4 + 1;
+  static constexpr int BAR_OFFSET = RED_OFFSET + 10 * 128 * 4;
+  // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[3], s_free[3],
+  // p_full[3], l_full[2], l_empty[2], o_done[3], o_final, o_empty, done, pair[4], decision[4][2]
+  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 31;
   static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t COL_S = 0, COL_O = 256, COL_P = 384;
+  // S buffers from column 0 (128 columns each), then O; with two S buffers P has its own
+  // 2 x 64 columns, with three each P_t (bf16 pairs) overwrites the first half of its S half
+  static constexpr int NB = KT_FA_SBUF;
+  static_assert(NB == 2 || NB == 3, "S buffers");
+  static constexpr uint32_t COL_S = 0, COL_O = NB * 128, COL_P = 384;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -139,6 +154,23 @@ __device__ __forceinline__ void ex2_h2(float x0, float x1, float& p0, float& p1)
 }
 
 // Pack two fp32 values into bf16x2 (round to nearest even); `lo` in the low half.
+// (d0, d1) = (a0, a1) * (b, b) + (c, c) as one packed fp32 instruction
+__device__ __forceinline__ void fma2_bc(float& d0, float& d1, float a0, float a1, float b, float c) {
+  uint64_t d, a, bb, cc;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(bb) : "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(cc) : "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(bb), "l"(cc));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+// (d0, d1) += (a0, a1) as one packed fp32 instruction
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
+  uint64_t d, a;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(d0), "f"(d1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(a));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -193,18 +225,26 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   auto v_full = [&](int s) { return bar0 + 8u * (4 + 2 * STAGES + s); };
   auto v_empty = [&](int s) { return bar0 + 8u * (4 + 2 * STAGES + VSTAGES + s); };
   constexpr int R = 4 + 2 * STAGES + 2 * VSTAGES;
+  constexpr int NB = CF::NB;
+  static_assert(NB == 2 || (KT_FA_ISSUERS == 2 && !KT_FA_ALT && !KT_FA_RELOAD),
+                "P over S: two issuers, column-half softmax keeping the scores in registers");
+  // tile t uses S buffer sbuf(t); sph(t) is the phase parity of that buffer's barriers for tile t
+  auto sbuf = [](int t) { return NB == 2 ? (t & 1) : t % NB; };
+  auto sph = [](int t) { return (uint32_t)((NB == 2 ? (t >> 1) : t / NB) & 1); };
   auto s_full = [&](int b) { return bar0 + 8u * (R + b); };
-  auto s_free = [&](int b) { return bar0 + 8u * (R + 2 + b); };
-  auto p_full = [&](int b) { return bar0 + 8u * (R + 4 + b); };
-  auto l_full = [&](int b) { return bar0 + 8u * (R + 6 + b); };
-  auto l_empty = [&](int b) { return bar0 + 8u * (R + 8 + b); };
-  const uint32_t o_done = bar0 + 8u * (R + 10);   // one phase per P·V product (two issuers: even tiles only)
-  // two issuers: o_done_of(t) completes once per P_t·V of tile parity t&1
-  auto o_done_of = [&](int t) { return (t & 1) ? bar0 + 8u * (R + 18) : o_done; };
-  const uint32_t o_final = bar0 + 8u * (R + 11);  // one phase per item: its last P·V product landed
-  const uint32_t o_empty = bar0 + 8u * (R + 12);  // one phase per item: the epilogue has read O
-  const uint32_t done_bar = bar0 + 8u * (R + 13);
-  const uint32_t pair_bar0 = bar0 + 8u * (R + 14);  // 4 softmax warp-pair exchanges
+  auto s_free = [&](int b) { return bar0 + 8u * (R + 3 + b); };
+  auto p_full = [&](int b) { return bar0 + 8u * (R + 6 + b); };
+  auto l_full = [&](int b) { return bar0 + 8u * (R + 9 + b); };
+  auto l_empty = [&](int b) { return bar0 + 8u * (R + 11 + b); };
+  const uint32_t o_done = bar0 + 8u * (R + 13);  // one issuer: one phase per P·V product
+  // two issuers: o_done_of(t) completes once per P_t·V of the tiles using S buffer sbuf(t)
+  auto o_done_of = [&](int t) { return bar0 + 8u * (R + 13 + sbuf(t)); };
+  const uint32_t o_final = bar0 + 8u * (R + 16);  // one phase per item: its last P·V product landed
+  const uint32_t o_empty = bar0 + 8u * (R + 17);  // one phase per item: the epilogue has read O
+  const uint32_t done_bar = bar0 + 8u * (R + 18);
+  const uint32_t pair_bar0 = bar0 + 8u * (R + 19);  // 4 softmax warp-pair exchanges
+  // alternate tiles: the running-max decision of tile parity p for lane quarter q
+  auto dec_bar = [&](int q, int p) { return bar0 + 8u * (R + 23 + 2 * q + p); };
   const uint32_t tmem_slot = bar0 + 8u * CF::NUM_BARS;
   const volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<const volatile uint32_t*>(base_ptr + CF::BAR_OFFSET + 8 * CF::NUM_BARS);
@@ -217,11 +257,15 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     for (int s = 0; s < 2; ++s) {
       mbar_init(q_full(s), 1);
       mbar_init(q_empty(s), 1);
-      mbar_init(s_full(s), 1);
-      mbar_init(s_free(s), SOFTMAX_THREADS);
-      mbar_init(p_full(s), SOFTMAX_THREADS);
       mbar_init(l_full(s), SOFTMAX_THREADS);
       mbar_init(l_empty(s), EPI_THREADS);
+    }
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(s_full(s), 1);
+      // alternate tiles: only the four warps of parity s use S / P buffer s
+      mbar_init(s_free(s), KT_FA_ALT ? SOFTMAX_THREADS / 2 : SOFTMAX_THREADS);
+      mbar_init(p_full(s), KT_FA_ALT ? SOFTMAX_THREADS / 2 : SOFTMAX_THREADS);
+      mbar_init(o_done_of(s), 1);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(k_full(s), 1);
@@ -231,12 +275,14 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       mbar_init(v_full(s), 1);
       mbar_init(v_empty(s), 1);
     }
-    mbar_init(o_done, 1);
-    mbar_init(o_done_of(1), 1);
     mbar_init(o_final, 1);
     mbar_init(o_empty, EPI_THREADS);
     mbar_init(done_bar, KT_FA_ISSUERS);
     for (int q = 0; q < 4; ++q) mbar_init(pair_bar0 + 8u * q, 64);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(dec_bar(q, 0), 32);
+      mbar_init(dec_bar(q, 1), 32);
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -331,30 +377,33 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       auto issue_s = [&](int t, int qb) {
         const uint32_t q_lo = q_lo0 + (uint32_t)qb * (CF::Q_BYTES >> 4);
         const uint32_t k_lo = k_lo0 + (uint32_t)(kc % STAGES) * (CF::K_BYTES >> 4);
-        const uint32_t d_tmem = tmem + CF::COL_S + (uint32_t)((t & 1) * BN);
+        const uint32_t d_tmem = tmem + CF::COL_S + (uint32_t)(sbuf(t) * BN);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(((kk >> 2) * CF::SLAB + (kk & 3) * 32) >> 4);
           mma_f16_ss_w(d_tmem, q_lo + off, k_hi, k_lo + off, k_hi, idesc_s, kk > 0 ? 1u : 0u);
         }
-        mma_commit(s_full(t & 1));
+        mma_commit(s_full(sbuf(t)));
         mma_commit(k_empty(kc % STAGES));  // the K slot is free once S_t has read it
         ++kc;
       };
       // O += P_t·V (O = P_t·V for the first tile of an item); needs P_t and the V tile
       auto pv_step = [&](int t, int k, bool first, bool last) -> bool {
-        if (!mbar_wait(p_full(t & 1), (uint32_t)(t >> 1) & 1u)) return false;
+        if (!mbar_wait(p_full(sbuf(t)), sph(t))) return false;
         if (!mbar_wait(v_full(vc % VSTAGES), (uint32_t)(vc / VSTAGES) & 1u)) return false;
         // the epilogue must have read the previous item's O before it is overwritten
         if (first && !mbar_wait(o_empty, ((uint32_t)k & 1u) ^ 1u)) return false;
         tc_fence_after();
         const uint32_t v_lo = v_lo0 + (uint32_t)(vc % VSTAGES) * (CF::V_BYTES >> 4);
-        const uint32_t p_tmem = tmem + CF::COL_P + (uint32_t)((t & 1) * 64);
+        // P_t: 64 columns of its own (two S buffers) or over the S tile, keys 64h.. at column 64h
+        const uint32_t p_tmem = NB == 2 ? tmem + CF::COL_P + (uint32_t)((t & 1) * 64)
+                                        : tmem + CF::COL_S + (uint32_t)(sbuf(t) * BN);
         const uint32_t o_tmem = tmem + CF::COL_O;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // 16 keys per MMA: rows 16kk..16kk+15 of every 64-column V slab; slabs CF::SLAB apart
-          mma_f16_ts_w(o_tmem, p_tmem + (uint32_t)(kk * 8), v_lo + (uint32_t)(kk * 16 * 128 / 16), v_hi, idesc_o,
+          const uint32_t p_col = NB == 2 ? (uint32_t)(kk * 8) : (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
+          mma_f16_ts_w(o_tmem, p_tmem + p_col, v_lo + (uint32_t)(kk * 16 * 128 / 16), v_hi, idesc_o,
                        (!first || kk > 0) ? 1u : 0u);
         }
         mma_commit(KT_FA_ISSUERS == 2 ? o_done_of(t) : o_done);
@@ -364,9 +413,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         return true;
       };
       // Two issuers: warp 1 issues S_t as soon as its K tile and S buffer are free
-      // and P_{t-2}·V is complete (then the softmax's parity waits on o_done_of
-      // are exact: at tile t at most P_{t-1}·V is outstanding); warp PV_WARP
-      // issues P_t·V as soon as P_t is in TMEM. One issuer: the order below.
+      // and P_{t-NB}·V, the last reader of the P columns tile t reuses, is
+      // complete (then the softmax's parity waits on o_done_of are exact: at tile
+      // t at most P_{t-1}·V is outstanding); warp PV_WARP issues P_t·V as soon as
+      // P_t is in TMEM. One issuer: the order below.
       if (KT_FA_ISSUERS == 2) {
         int t = 0, k = 0;
         for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
@@ -380,8 +430,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           for (int j = 0; j < n_kv; ++j, ++t) {
             if (s_issuer) {
               if (!mbar_wait(k_full(kc % STAGES), (uint32_t)(kc / STAGES) & 1u) ||
-                  !mbar_wait(s_free(t & 1), ((uint32_t)(t >> 1) & 1u) ^ 1u) ||
-                  (t >= 2 && !mbar_wait(o_done_of(t - 2), (uint32_t)((t - 2) >> 1) & 1u))) {
+                  !mbar_wait(s_free(sbuf(t)), sph(t) ^ 1u) ||
+                  (t >= NB && !mbar_wait(o_done_of(t - NB), sph(t - NB)))) {
                 timed_out = true;
                 break;
               }
@@ -436,6 +486,171 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       (void)s_issuer;
       (void)pv_issuer;
     }
+  } else if (KT_FA_ALT && warp < V_LOADER_WARP) {
+    // softmax, alternate tiles: the warp of lane quarter q = warp & 3 and parity h
+    // takes the S tiles t with t % 2 == h, all 128 key columns of its 32 rows. The
+    // running max a tile's exponentials use is decided right after the tile's row
+    // maxima are known and published to the other parity's warp of the quarter,
+    // which waits for that decision before its next tile: the exponentials of
+    // consecutive tiles then overlap on the two warps of a scheduler instead of
+    // running in lockstep. Each warp keeps its own row-sum share relative to the
+    // last maximum it used; the epilogue brings both shares to the final maximum.
+    const int quarter = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float* m_sh = red;              // [2 item parity][128]
+    float* l_hand = red + 2 * 128;  // [2 item parity][2 parity][128]
+    float* m_hand = red + 6 * 128;  // [2 item parity][2 parity][128]
+    constexpr int HD4 = D;          // O columns this thread rescales (its whole row)
+    int t = 0, k = 0;
+    for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
+      int qt, bh;
+      item_coords<CAUSAL>(w, num_q_tiles, BH, qt, bh);
+      const int n_kv = kv_tiles<CAUSAL>(qt, S);
+      const int q0 = qt * BM;
+      const int qrow = q0 + row;
+      float my_m = -INFINITY;  // the maximum l_part is relative to
+      float l_part = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++t) {
+        if ((t & 1) != h) continue;
+        // the decision of tile t-1 (made by the other parity's warp of this quarter)
+        if (t > 0 && !__all_sync(0xffffffffu, mbar_wait(dec_bar(quarter, (t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u))) {
+          timed_out = true;
+          break;
+        }
+        const float m_prev = (j == 0) ? -INFINITY : m_sh[(k & 1) * 128 + row];
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full(h), (uint32_t)(t >> 1) & 1u))) {
+          timed_out = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(h * BN);
+        const int key0 = j * BN;
+        const bool mask_tile = (CAUSAL && j * BN + BN - 1 > q0) || (j * BN + BN > S);
+        auto mask32 = [&](uint32_t (&v)[32], int c) {
+          if (mask_tile) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int key = key0 + c + i;
+              if (!(key < S && (!CAUSAL || key <= qrow))) v[i] = __float_as_uint(-INFINITY);
+            }
+          }
+        };
+        // row maximum over the 128 keys, two 32-column loads in flight at a time
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t va[32], vb[32];
+          tmem_ld32(s_addr + (uint32_t)c, va);
+          tmem_ld32(s_addr + (uint32_t)(c + 32), vb);
+          tmem_ld_wait();
+          mask32(va, c);
+          mask32(vb, c + 32);
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], fmaxf(__uint_as_float(va[i]), __uint_as_float(vb[i])));
+          mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        }
+        const float m_tile = mx * scale_log2;
+        const bool raise = m_tile > m_prev + kRescaleThreshold;
+        const float m_new = raise ? m_tile : m_prev;
+        m_sh[(k & 1) * 128 + row] = m_new;
+        mbar_arrive(dec_bar(quarter, t & 1));  // release: m_sh is visible to the waiting warp
+        // O holds P_0..P_{j-1}·V of this item under m_prev: rescale the raised rows
+        if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          const float alpha = raise ? ((m_prev == -INFINITY) ? 0.f : ex2(m_prev - m_new)) : 1.f;
+          const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), sph(t - 1))
+                                                  : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
+          if (!__all_sync(0xffffffffu, o_ready)) {
+            timed_out = true;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < HD4; c += 32) {
+            uint32_t v[32];
+            const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)c;
+            tmem_ld32(oa, v);
+            tmem_ld_wait();
+            uint32_t w0[16], w1[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              w0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              w1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
+            }
+            tmem_st16(oa, w0);
+            tmem_st16(oa + 16u, w1);
+          }
+          tmem_st_wait();
+        }
+        // this warp's row-sum share follows the maximum
+        if (my_m != m_new) {
+          l_part = (my_m == -INFINITY) ? 0.f : l_part * ex2(my_m - m_new);
+          my_m = m_new;
+        }
+        // p = 2^(s·c − m_new) into P buffer h (bf16, 64 columns); scores reloaded 32 columns at a time,
+        // the next chunk's load in flight while the current one is exponentiated
+        const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(h * 64);
+        auto exp_chunk = [&](const uint32_t (&sc)[32], int c, auto poly_tag) -> float {
+          constexpr bool POLY = decltype(poly_tag)::value;
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float x0, x1;
+            if (KT_FA_X2) {
+              fma2_bc(x0, x1, __uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), scale_log2, -m_new);
+            } else {
+              x0 = fmaf(__uint_as_float(sc[2 * i]), scale_log2, -m_new);
+              x1 = fmaf(__uint_as_float(sc[2 * i + 1]), scale_log2, -m_new);
+            }
+            float p0, p1;
+            if (KT_FA_EXP16) {
+              ex2_h2(x0, x1, p0, p1);
+            } else if (POLY && (i & 3) == 3) {
+              p0 = ex2_poly(x0);
+              p1 = ex2_poly(x1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            if (KT_FA_X2) add2(s4[(i & 1) * 2], s4[(i & 1) * 2 + 1], p0, p1);
+            else s4[i & 3] += p0 + p1;
+            pk[i] = pack_bf16(p0, p1);
+          }
+          tmem_st16(p_addr + (uint32_t)(c / 2), pk);
+          return (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        };
+        auto exp_row = [&](auto poly_tag) -> float {
+          float sum = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t sc[32];
+            tmem_ld32(s_addr + (uint32_t)c, sc);
+            tmem_ld_wait();
+            mask32(sc, c);
+            sum += exp_chunk(sc, c, poly_tag);
+          }
+          return sum;
+        };
+        l_part += (KT_FA_POLY && !mask_tile) ? exp_row(std::true_type{}) : exp_row(std::false_type{});
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(s_free(h));
+        mbar_arrive(p_full(h));
+      }
+      if (timed_out) break;
+      // hand this warp's share and its maximum to the epilogue (two slots, by item parity)
+      const int lb = k & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(l_empty(lb), ((uint32_t)(k >> 1) & 1u) ^ 1u))) {
+        timed_out = true;
+        break;
+      }
+      l_hand[(lb * 2 + h) * 128 + row] = l_part;
+      m_hand[(lb * 2 + h) * 128 + row] = my_m;
+      mbar_arrive(l_full(lb));
+    }
   } else if (warp < V_LOADER_WARP) {
     // softmax: TMEM lane quarter = warp % 4, the two warps of a quarter split the columns
     const int quarter = warp & 3;
@@ -455,13 +670,14 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       float m_run = -INFINITY;  // running max of s·scale·log2e used by the exponentials (same in both halves)
       float l_part = 0.f;       // this half's share of the row sum
       for (int j = 0; j < n_kv; ++j, ++t) {
-        const int b = t & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(s_full(b), (uint32_t)(t >> 1) & 1u))) {
+        const int b = t & 1;       // tile parity: the max-exchange slots
+        const int sb = sbuf(t);    // S (and P) buffer
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full(sb), sph(t)))) {
           timed_out = true;
           break;
         }
         tc_fence_after();
-        const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(b * BN + half * HC);
+        const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(sb * BN + half * HC);
         const int key0 = j * BN + half * HC;
         const bool mask_tile = (CAUSAL && j * BN + BN - 1 > q0) || (j * BN + BN > S);
         uint32_t sv[HC];
@@ -484,7 +700,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         float* red_max = red + (b * 2) * 128;
         red_max[half * 128 + row] = mh;
         mbar_arrive(pair_mbar);  // release: the write above is visible to the partner after its wait
-        const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2));
+        const uint32_t p_addr = NB == 2 ? tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2))
+                                        : s_addr;  // over this half's scores, which are in registers
         // p = 2^(s·c − m) (masked entries are −inf -> 0) into TMEM as bf16; returns this half's sum.
         // The polynomial share is chosen per tile (masked tiles use MUFU only).
         auto make_p = [&](float m, auto poly_tag) -> float {
@@ -511,8 +728,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             }
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float x0 = fmaf(__uint_as_float(sc[2 * i]), scale_log2, -m);
-              const float x1 = fmaf(__uint_as_float(sc[2 * i + 1]), scale_log2, -m);
+              float x0, x1;
+              if (KT_FA_X2) {
+                fma2_bc(x0, x1, __uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), scale_log2, -m);
+              } else {
+                x0 = fmaf(__uint_as_float(sc[2 * i]), scale_log2, -m);
+                x1 = fmaf(__uint_as_float(sc[2 * i + 1]), scale_log2, -m);
+              }
               float p0, p1;
               if (KT_FA_EXP16) {
                 ex2_h2(x0, x1, p0, p1);
@@ -523,7 +745,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
                 p0 = ex2(x0);
                 p1 = ex2(x1);
               }
-              s4[i & 3] += p0 + p1;
+              if (KT_FA_X2) add2(s4[(i & 1) * 2], s4[(i & 1) * 2 + 1], p0, p1);
+              else s4[i & 3] += p0 + p1;
               pk[i] = pack_bf16(p0, p1);
             }
             tmem_st16(p_addr + (uint32_t)(c / 2), pk);
@@ -570,11 +793,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             l_part *= alpha;
           }
           // O holds P_0..P_{j-1}·V of this item: rescale this half of it once the
-          // previous P·V product has landed. o_done has completed t-1 or t phases
-          // here (s_full of tile t was committed after P_{t-2}·V was issued, and
-          // P_t·V needs this thread's P_t), so a parity wait is exact.
+          // previous P·V product has landed. The o_done barrier of P_{t-1}·V has
+          // completed P_{t-1-NB}·V (issued before P_{t-NB}·V, which S_t waited for)
+          // and cannot complete P_{t-1+NB}·V (it needs this thread's P), so a
+          // parity wait is exact.
           if (j > 0 && __any_sync(0xffffffffu, raise)) {
-            const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), (uint32_t)((t - 1) >> 1) & 1u)
+            const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), sph(t - 1))
                                                     : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
             if (!__all_sync(0xffffffffu, o_ready)) {
               timed_out = true;
@@ -602,8 +826,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(s_free(b));
-        mbar_arrive(p_full(b));
+        mbar_arrive(s_free(sb));
+        mbar_arrive(p_full(sb));
       }
       if (timed_out) break;
       // hand this half's row sum to the epilogue warps (two slots, by item parity)
@@ -631,7 +855,16 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         timed_out = true;
         break;
       }
-      const float l_run = red[(4 + 2 * lb) * 128 + row] + red[(5 + 2 * lb) * 128 + row];
+      float l_run;
+      if (KT_FA_ALT) {
+        // both parities' shares, each relative to the last maximum its warp used, at the final maximum
+        const float ma = red[(6 + lb * 2) * 128 + row], mb = red[(7 + lb * 2) * 128 + row];
+        const float la = red[(2 + lb * 2) * 128 + row], lbs = red[(3 + lb * 2) * 128 + row];
+        const float mf = fmaxf(ma, mb);
+        l_run = (ma == -INFINITY ? 0.f : la * ex2(ma - mf)) + (mb == -INFINITY ? 0.f : lbs * ex2(mb - mf));
+      } else {
+        l_run = red[(4 + 2 * lb) * 128 + row] + red[(5 + 2 * lb) * 128 + row];
+      }
       mbar_arrive(l_empty(lb));
       tc_fence_after();
       const float inv = 1.0f / l_run;

@@ -137,11 +137,16 @@ def test_naive_attention_matches(dev, lib):
 
 
 @pytest.mark.parametrize("params", [{"kind": 2, "order": 0}, {"kind": 2, "order": 1, "exp16": 1},
-                                    {"kind": 1, "exp16": 1}, {"kind": 1, "poly_exp2": 1}])
+                                    {"kind": 1, "exp16": 1}, {"kind": 1, "poly_exp2": 1},
+                                    {"kind": 1, "alt": 1}, {"kind": 1, "alt": 1, "issuers": 1},
+                                    {"kind": 1, "alt": 0}, {"kind": 1, "sbuf": 3}, {"kind": 1, "sbuf": 2},
+                                    {"kind": 1, "sbuf": 3, "x2": 1, "poly_exp2": 1}])
 def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
-    """Non-default kernels of the tuner's attention axes, built as variant
-    libraries: the two-query-tile ping-pong kernel (both MMA issue orders) and
-    the half-precision / polynomial exponentials, against the oracle."""
+    """Kernels of the tuner's attention axes, built as variant libraries: the
+    two-query-tile ping-pong kernel (both MMA issue orders), the half-precision /
+    polynomial exponentials, both softmax splits (column halves, alternate
+    tiles) and two or three S buffers in TMEM (P in its own columns or over its
+    S tile), against the oracle, including scores whose running max rises."""
     monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
     import generator
     ok, log, so = generator.ensure_variant("attention", params)
@@ -152,4 +157,12 @@ def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
         for causal in (False, True):
             o = run(v, dev, inp["q"], inp["k"], inp["v"], inp["scale"], causal)
             assert ref.normwise_rel_err(o, oracle(inp["q"], inp["k"], inp["v"], inp["scale"], causal)) <= TOL
+    rng = np.random.default_rng(8)
+    B, H, S, D = 1, 6, 1024, 128
+    q = rng.standard_normal((B, H, S, D), dtype=np.float32) * 3.0
+    k = rng.standard_normal((B, H, S, D), dtype=np.float32) * np.linspace(0.2, 3.0, S, dtype=np.float32)[:, None]
+    qb, kb, vb = (workloads.bf16_bits(a) for a in (q, k, rng.standard_normal((B, H, S, D), dtype=np.float32)))
+    for causal in (False, True):
+        o = run(v, dev, qb, kb, vb, 1.0 / math.sqrt(D), causal)
+        assert ref.normwise_rel_err(o, oracle(qb, kb, vb, 1.0 / math.sqrt(D), causal)) <= TOL
     assert v.device_error() == 0
