@@ -62,6 +62,16 @@
 #ifndef KT_FA_X2
 #define KT_FA_X2 0  // 1: the exponent arguments and row sums in packed fma.rn.f32x2 / add.rn.f32x2
 #endif
+#ifndef KT_FA_WARP_ARRIVE
+#define KT_FA_WARP_ARRIVE 0  // 1: one arrival per warp (after __syncwarp) on the softmax / epilogue mbarriers
+#endif
+#ifndef KT_FA_SPEC0
+#define KT_FA_SPEC0 0  // 1: an item's first tile also speculates, on the previous item's final running max
+#endif
+#ifndef KT_FA_DEPHASE
+#define KT_FA_DEPHASE 0  // clocks the second softmax warp of each lane quarter starts its first tile late
+                         // (exponential phases of the two warps of a scheduler offset, not coinciding)
+#endif
 #ifndef KT_FA_SPEC
 #define KT_FA_SPEC 1  // 1: exponentials start with the running max before the partner's half max is read
 #endif
@@ -85,6 +95,7 @@ constexpr int PV_WARP = V_LOADER_WARP + 1 + EPI_THREADS / 32;  // warp 15 (two i
 constexpr int THREADS = 96 + 32 * SOFTMAX_WARPS + EPI_THREADS + (KT_FA_ISSUERS == 2 ? 32 : 0);
 constexpr int SOFTMAX_THREADS = 32 * SOFTMAX_WARPS;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: O is rescaled only when the max grows by > 2^8
+constexpr float kGuessSlack = 64.0f;       // log2 units: a first-tile guess may exceed the row max by this much
 constexpr int kHeadGroup = 8;              // causal scheduling: heads whose K/V share L2
 
 template <int D, int STAGES, int VSTAGES = KT_FA_VSTAGES>
@@ -226,8 +237,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   auto v_empty = [&](int s) { return bar0 + 8u * (4 + 2 * STAGES + VSTAGES + s); };
   constexpr int R = 4 + 2 * STAGES + 2 * VSTAGES;
   constexpr int NB = CF::NB;
-  static_assert(NB == 2 || (KT_FA_ISSUERS == 2 && !KT_FA_ALT && !KT_FA_RELOAD),
-                "P over S: two issuers, column-half softmax keeping the scores in registers");
+  static_assert(NB == 2 || (KT_FA_ISSUERS == 2 && !KT_FA_RELOAD),
+                "P over S: two issuers, scores not reloaded after P is written");
   // tile t uses S buffer sbuf(t); sph(t) is the phase parity of that buffer's barriers for tile t
   auto sbuf = [](int t) { return NB == 2 ? (t & 1) : t % NB; };
   auto sph = [](int t) { return (uint32_t)((NB == 2 ? (t >> 1) : t / NB) & 1); };
@@ -253,18 +264,30 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   const int num_q_tiles = (S + BM - 1) / BM;
   const int num_items = BH * num_q_tiles;
 
+  // arrivals per warp on the barriers the softmax and epilogue warps signal: every
+  // thread, or lane 0 after the warp has synchronised (its writes are ordered
+  // before lane 0's release by __syncwarp)
+  constexpr int AW = KT_FA_WARP_ARRIVE ? 1 : 32;
+  auto warp_arrive = [&](uint32_t bar) {
+    if (KT_FA_WARP_ARRIVE) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar);
+    } else {
+      mbar_arrive(bar);
+    }
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(q_full(s), 1);
       mbar_init(q_empty(s), 1);
-      mbar_init(l_full(s), SOFTMAX_THREADS);
-      mbar_init(l_empty(s), EPI_THREADS);
+      mbar_init(l_full(s), SOFTMAX_WARPS * AW);
+      mbar_init(l_empty(s), EPI_THREADS / 32 * AW);
     }
     for (int s = 0; s < NB; ++s) {
       mbar_init(s_full(s), 1);
-      // alternate tiles: only the four warps of parity s use S / P buffer s
-      mbar_init(s_free(s), KT_FA_ALT ? SOFTMAX_THREADS / 2 : SOFTMAX_THREADS);
-      mbar_init(p_full(s), KT_FA_ALT ? SOFTMAX_THREADS / 2 : SOFTMAX_THREADS);
+      // alternate tiles: only the four warps of the tile's parity use its S / P buffer
+      mbar_init(s_free(s), (KT_FA_ALT ? SOFTMAX_WARPS / 2 : SOFTMAX_WARPS) * AW);
+      mbar_init(p_full(s), (KT_FA_ALT ? SOFTMAX_WARPS / 2 : SOFTMAX_WARPS) * AW);
       mbar_init(o_done_of(s), 1);
     }
     for (int s = 0; s < STAGES; ++s) {
@@ -276,12 +299,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       mbar_init(v_empty(s), 1);
     }
     mbar_init(o_final, 1);
-    mbar_init(o_empty, EPI_THREADS);
+    mbar_init(o_empty, EPI_THREADS / 32 * AW);
     mbar_init(done_bar, KT_FA_ISSUERS);
-    for (int q = 0; q < 4; ++q) mbar_init(pair_bar0 + 8u * q, 64);
+    for (int q = 0; q < 4; ++q) mbar_init(pair_bar0 + 8u * q, 2 * AW);
     for (int q = 0; q < 4; ++q) {
-      mbar_init(dec_bar(q, 0), 32);
-      mbar_init(dec_bar(q, 1), 32);
+      mbar_init(dec_bar(q, 0), AW);
+      mbar_init(dec_bar(q, 1), AW);
     }
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
@@ -402,7 +425,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // 16 keys per MMA: rows 16kk..16kk+15 of every 64-column V slab; slabs CF::SLAB apart
-          const uint32_t p_col = NB == 2 ? (uint32_t)(kk * 8) : (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
+          // P over S from column halves: keys 64h.. at column 64h; otherwise keys in order
+          const uint32_t p_col =
+              (NB == 2 || KT_FA_ALT) ? (uint32_t)(kk * 8) : (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
           mma_f16_ts_w(o_tmem, p_tmem + p_col, v_lo + (uint32_t)(kk * 16 * 128 / 16), v_hi, idesc_o,
                        (!first || kk > 0) ? 1u : 0u);
         }
@@ -520,12 +545,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           break;
         }
         const float m_prev = (j == 0) ? -INFINITY : m_sh[(k & 1) * 128 + row];
-        if (!__all_sync(0xffffffffu, mbar_wait(s_full(h), (uint32_t)(t >> 1) & 1u))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full(sbuf(t)), sph(t)))) {
           timed_out = true;
           break;
         }
         tc_fence_after();
-        const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(h * BN);
+        const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(sbuf(t) * BN);
         const int key0 = j * BN;
         const bool mask_tile = (CAUSAL && j * BN + BN - 1 > q0) || (j * BN + BN > S);
         auto mask32 = [&](uint32_t (&v)[32], int c) {
@@ -556,7 +581,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const bool raise = m_tile > m_prev + kRescaleThreshold;
         const float m_new = raise ? m_tile : m_prev;
         m_sh[(k & 1) * 128 + row] = m_new;
-        mbar_arrive(dec_bar(quarter, t & 1));  // release: m_sh is visible to the waiting warp
+        warp_arrive(dec_bar(quarter, t & 1));  // release: m_sh is visible to the waiting warp
         // O holds P_0..P_{j-1}·V of this item under m_prev: rescale the raised rows
         if (j > 0 && __any_sync(0xffffffffu, raise)) {
           const float alpha = raise ? ((m_prev == -INFINITY) ? 0.f : ex2(m_prev - m_new)) : 1.f;
@@ -591,7 +616,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         }
         // p = 2^(s·c − m_new) into P buffer h (bf16, 64 columns); scores reloaded 32 columns at a time,
         // the next chunk's load in flight while the current one is exponentiated
-        const uint32_t p_addr = tmem + lane_off + CF::COL_P + (uint32_t)(h * 64);
+        // P: 64 columns of its own, or over the scores (chunk c's P lands in columns c/2..c/2+15,
+        // all of them already read)
+        const uint32_t p_addr = NB == 2 ? tmem + lane_off + CF::COL_P + (uint32_t)(h * 64) : s_addr;
         auto exp_chunk = [&](const uint32_t (&sc)[32], int c, auto poly_tag) -> float {
           constexpr bool POLY = decltype(poly_tag)::value;
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -637,8 +664,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         l_part += (KT_FA_POLY && !mask_tile) ? exp_row(std::true_type{}) : exp_row(std::false_type{});
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(s_free(h));
-        mbar_arrive(p_full(h));
+        warp_arrive(s_free(sbuf(t)));
+        warp_arrive(p_full(sbuf(t)));
       }
       if (timed_out) break;
       // hand this warp's share and its maximum to the epilogue (two slots, by item parity)
@@ -649,7 +676,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       }
       l_hand[(lb * 2 + h) * 128 + row] = l_part;
       m_hand[(lb * 2 + h) * 128 + row] = my_m;
-      mbar_arrive(l_full(lb));
+      warp_arrive(l_full(lb));
     }
   } else if (warp < V_LOADER_WARP) {
     // softmax: TMEM lane quarter = warp % 4, the two warps of a quarter split the columns
@@ -660,6 +687,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
     const uint32_t pair_mbar = pair_bar0 + 8u * (uint32_t)quarter;  // mbarrier of the two warps of this quarter
     constexpr int HC = BN / 2;                                     // score columns per thread
     constexpr int HD = D / 2;                                      // O columns per thread (rescale)
+    float m_guess = -INFINITY;  // the previous item's final running max (same in both halves)
     int t = 0, k = 0;
     for (int w = blockIdx.x; w < num_items && !timed_out; w += gridDim.x, ++k) {
       int qt, bh;
@@ -667,8 +695,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       const int n_kv = kv_tiles<CAUSAL>(qt, S);
       const int q0 = qt * BM;
       const int qrow = q0 + row;
-      float m_run = -INFINITY;  // running max of s·scale·log2e used by the exponentials (same in both halves)
-      float l_part = 0.f;       // this half's share of the row sum
+      // running max of s·scale·log2e used by the exponentials (same in both halves); with
+      // first-tile speculation it starts at the previous item's value until the exchange
+      float m_run = KT_FA_SPEC0 ? m_guess : -INFINITY;
+      float l_part = 0.f;  // this half's share of the row sum
       for (int j = 0; j < n_kv; ++j, ++t) {
         const int b = t & 1;       // tile parity: the max-exchange slots
         const int sb = sbuf(t);    // S (and P) buffer
@@ -677,6 +707,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           break;
         }
         tc_fence_after();
+        if (KT_FA_DEPHASE > 0 && half == 1 && t == 0) {
+          // once, after the first scores landed: the second warp of the pair starts late
+          const long long c0 = clock64();
+          while (clock64() - c0 < KT_FA_DEPHASE) {
+          }
+        }
         const uint32_t s_addr = tmem + lane_off + CF::COL_S + (uint32_t)(sb * BN + half * HC);
         const int key0 = j * BN + half * HC;
         const bool mask_tile = (CAUSAL && j * BN + BN - 1 > q0) || (j * BN + BN > S);
@@ -699,7 +735,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // tile parity: the partner may still read the previous tile's slot)
         float* red_max = red + (b * 2) * 128;
         red_max[half * 128 + row] = mh;
-        mbar_arrive(pair_mbar);  // release: the write above is visible to the partner after its wait
+        warp_arrive(pair_mbar);  // release: the write above is visible to the partner after its wait
         const uint32_t p_addr = NB == 2 ? tmem + lane_off + CF::COL_P + (uint32_t)(b * 64 + half * (HC / 2))
                                         : s_addr;  // over this half's scores, which are in registers
         // p = 2^(s·c − m) (masked entries are −inf -> 0) into TMEM as bf16; returns this half's sum.
@@ -763,7 +799,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // Only if the partner's half then asks for a raise are P and the sum redone
         // below with the new maximum (the MMA reads P only after p_full).
         bool pair_seen = false, finished = false;
-        if (KT_FA_SPEC && j > 0 && !__any_sync(0xffffffffu, mh * scale_log2 > m_run + kRescaleThreshold)) {
+        // a first-tile guess must neither be exceeded by more than the threshold nor
+        // exceed the row max by more than kGuessSlack (P would lose its range)
+        auto guess_bad = [&](float mxs) {
+          return mxs > m_run + kRescaleThreshold || (j == 0 && mxs < m_run - kGuessSlack);
+        };
+        if (KT_FA_SPEC && (j > 0 || (KT_FA_SPEC0 && __all_sync(0xffffffffu, m_run != -INFINITY))) &&
+            !__any_sync(0xffffffffu, guess_bad(mh * scale_log2))) {
           const float spec_sum = p_sum(m_run);
           if (!__all_sync(0xffffffffu, mbar_wait(pair_mbar, (uint32_t)t & 1u))) {
             timed_out = true;
@@ -771,7 +813,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           }
           pair_seen = true;
           const float mx_s = fmaxf(red_max[row], red_max[128 + row]);
-          if (!__any_sync(0xffffffffu, mx_s * scale_log2 > m_run + kRescaleThreshold)) {
+          if (!__any_sync(0xffffffffu, guess_bad(mx_s * scale_log2))) {
             l_part += spec_sum;
             finished = true;
           } else {
@@ -785,6 +827,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           }
           const float mx = fmaxf(red_max[row], red_max[128 + row]);
           const float m_tile = mx * scale_log2;
+          // a first-tile guess the row maxima reject (in either half: both see the same
+          // maxima and take the same decision): start from the tile's max
+          if (j == 0 && __any_sync(0xffffffffu, guess_bad(m_tile))) m_run = -INFINITY;
           const bool raise = m_tile > m_run + kRescaleThreshold;
           float alpha = 1.f;
           if (raise) {
@@ -826,8 +871,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(s_free(sb));
-        mbar_arrive(p_full(sb));
+        warp_arrive(s_free(sb));
+        warp_arrive(p_full(sb));
       }
       if (timed_out) break;
       // hand this half's row sum to the epilogue warps (two slots, by item parity)
@@ -837,7 +882,8 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         break;
       }
       red[(4 + 2 * lb + half) * 128 + row] = l_part;
-      mbar_arrive(l_full(lb));
+      warp_arrive(l_full(lb));
+      m_guess = m_run;
     }
   } else {
     // epilogue warps: O / l -> bf16, one query row per thread; O is released to the
@@ -865,7 +911,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       } else {
         l_run = red[(4 + 2 * lb) * 128 + row] + red[(5 + 2 * lb) * 128 + row];
       }
-      mbar_arrive(l_empty(lb));
+      warp_arrive(l_empty(lb));
       tc_fence_after();
       const float inv = 1.0f / l_run;
       uint4* dst = reinterpret_cast<uint4*>(O + ((int64_t)bh * S + qrow) * D);
@@ -876,7 +922,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         tmem_ld_wait();
         if (c + 32 == D) {
           tc_fence_before();
-          mbar_arrive(o_empty);  // all of O is in registers: the next item may overwrite it
+          warp_arrive(o_empty);  // all of O is in registers: the next item may overwrite it
         }
         if (qrow < S) {
 #pragma unroll

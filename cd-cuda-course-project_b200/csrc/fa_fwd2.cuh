@@ -51,7 +51,9 @@
 #define KT_FA2_ORDER 0  // 0: ping-pong issue order (below); 1: in-phase order S_A(j), S_B(j), P_A(j-1)V, P_B(j-1)V
 #endif
 #ifndef KT_FA_EXP16
-#define KT_FA_EXP16 0  // 1: exponentials as packed half-precision pairs (ex2.approx.f16x2)
+#define KT_FA_EXP16 0  // 1: exponentials as packed half-precision pairs (ex2.approx.f16x2); not offered
+                       // by the tuner for this kernel: NaN on the first causal rows of heads whose
+                       // scores reach ~300 (log2 units)
 #endif
 #ifndef KT_FA2_POLY
 #define KT_FA2_POLY 0  // n > 0: every n-th pair of exponentials of a row is computed by a polynomial on the FMA pipe

@@ -233,6 +233,9 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["alt"] = [0, 1]             # kind 1: softmax warps of a lane quarter take alternate S tiles (1)
         space["sbuf"] = [2, 3]            # kind 1: S accumulators in TMEM (3: P written over its S tile)
         space["x2"] = [0, 1]              # kind 1: exponent arguments and row sums in packed f32x2 instructions
+        space["warp_arrive"] = [0, 1]     # kind 1: one mbarrier arrival per warp instead of per thread
+        space["spec0"] = [0, 1]           # kind 1: first tile of an item speculates on the previous item's max
+        space["dephase"] = [0, 400, 800]  # kind 1: clocks the second softmax warp of a scheduler starts late
         space["order"] = [0, 1]           # kind 2: MMA issue order (0 ping-pong, 1 in phase)
         space["poly_every"] = [0, 4, 8]   # kind 2: every n-th exponential pair on the FMA pipe (0: none)
         space["causal"] = [False, True]
@@ -288,15 +291,21 @@ def is_valid(kernel: str, params: dict) -> bool:
             and params.get("ffma_wide", 0) == 0
     if fam == "attention":
         if params.get("kind", 1) == 2:
+            # half-precision exponentials gave NaN on the first causal rows of heads whose
+            # scores reach ~300 (log2 units) in this kernel: not offered
+            if params.get("exp16", 0):
+                return False
             # the kind-1 axes do not shape this kernel: one representative point
             return (params.get("stages", 2), params.get("v_stages", 2), params.get("poly_exp2", 0),
-                    params.get("issuers", 2), params.get("alt", 0), params.get("sbuf", 2), params.get("x2", 0)) == (2, 2, 0, 2, 0, 2, 0)
+                    params.get("issuers", 2), params.get("alt", 0), params.get("sbuf", 2), params.get("x2", 0),
+                    params.get("warp_arrive", 0), params.get("spec0", 0),
+                    params.get("dephase", 0)) == (2, 2, 0, 2, 0, 2, 0, 0, 0, 0)
         if params.get("order", 0) != 0 or params.get("poly_every", 0) != 0:
             return False
-        if params.get("alt", 0) and (params.get("spec", 1) != 1 or params.get("reload", 0) != 0):
+        if params.get("alt", 0) and (params.get("spec", 1) != 1 or params.get("reload", 0) != 0
+                                     or params.get("spec0", 0) or params.get("dephase", 0)):
             return False  # whole-row softmax: the column-half exchange axes do not shape it
-        if params.get("sbuf", 2) == 3 and (params.get("issuers", 2) != 2 or params.get("alt", 0)
-                                           or params.get("reload", 0)):
+        if params.get("sbuf", 2) == 3 and (params.get("issuers", 2) != 2 or params.get("reload", 0)):
             return False  # P over S needs the two issuers and the scores kept in registers
         # head dim 128: two Q buffers + (K + V slots) x 32 KB must fit the 227 KB of shared memory
         return params.get("stages", 2) + params.get("v_stages", 2) <= 4
