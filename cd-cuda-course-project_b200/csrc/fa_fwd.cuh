@@ -54,16 +54,23 @@
                          // per instruction, above the 64-clock 128x128x16 MMA); 1: one issuing thread
 #endif
 #ifndef KT_FA_ALT
-#define KT_FA_ALT 0  // 1: the two softmax warps of a TMEM lane quarter take alternate S tiles, whole 128-key rows
+#define KT_FA_ALT 1  // 1: the two softmax warps of a TMEM lane quarter take alternate S tiles, whole 128-key
+                     // rows (their latency phases overlap the other warp's exponentials); 0: column halves
 #endif
 #ifndef KT_FA_SBUF
-#define KT_FA_SBUF 2  // S accumulators in TMEM: 2 (P in its own columns) or 3 (P written over its S tile)
+// S accumulators in TMEM: 2 (P in its own columns) or 3 (P written over its S tile; needs the two
+// issuers and scores that are not reloaded after P is written)
+#define KT_FA_SBUF ((KT_FA_ISSUERS == 2 && !KT_FA_RELOAD) ? 3 : 2)
 #endif
 #ifndef KT_FA_X2
-#define KT_FA_X2 0  // 1: the exponent arguments and row sums in packed fma.rn.f32x2 / add.rn.f32x2
+#define KT_FA_X2 1  // 1: the exponent arguments and row sums in packed fma.rn.f32x2 / add.rn.f32x2
 #endif
 #ifndef KT_FA_WARP_ARRIVE
 #define KT_FA_WARP_ARRIVE 0  // 1: one arrival per warp (after __syncwarp) on the softmax / epilogue mbarriers
+#endif
+#ifndef KT_FA_PSPLIT
+// alternate tiles: P_t·V issued in this many key ranges (1, 2 or 4), each once its P columns are stored
+#define KT_FA_PSPLIT (KT_FA_ALT ? 2 : 1)
 #endif
 #ifndef KT_FA_SPEC0
 #define KT_FA_SPEC0 0  // 1: an item's first tile also speculates, on the previous item's final running max
@@ -79,8 +86,7 @@
 #define KT_FA_RELOAD 0  // 1: the exponential pass reloads the scores from TMEM 32 columns at a time
 #endif
 #ifndef KT_FA_POLY
-#define KT_FA_POLY 0  // 1: every 4th value pair of exponentials on the FMA pipe (measured slower: the FMA/ALU
-                      // pipes, not MUFU, limit the softmax warps)
+#define KT_FA_POLY 1  // n = 1..3: n of every 4 value pairs of exponentials on the FMA pipe (polynomial)
 #endif
 
 namespace kt {
@@ -115,8 +121,9 @@ struct Cfg {
   static constexpr int RED_OFFSET = V_OFFSET + VSTAGES * V_BYTES;
   static constexpr int BAR_OFFSET = RED_OFFSET + 10 * 128 * 4;
   // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[3], s_free[3],
-  // p_full[3], l_full[2], l_empty[2], o_done[3], o_final, o_empty, done, pair[4], decision[4][2]
-  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 31;
+  // p_full[3], l_full[2], l_empty[2], o_done[3], o_final, o_empty, done, pair[4], decision[4][2],
+  // p_part[3][3]
+  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 31 + 9;
   static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
@@ -256,6 +263,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   const uint32_t pair_bar0 = bar0 + 8u * (R + 19);  // 4 softmax warp-pair exchanges
   // alternate tiles: the running-max decision of tile parity p for lane quarter q
   auto dec_bar = [&](int q, int p) { return bar0 + 8u * (R + 23 + 2 * q + p); };
+  // alternate tiles, P·V in KT_FA_PSPLIT key ranges: range i < KT_FA_PSPLIT-1 of buffer b is
+  // stored (the last range is signalled by p_full)
+  constexpr int PSPLIT = KT_FA_PSPLIT;
+  static_assert(PSPLIT == 1 || ((PSPLIT == 2 || PSPLIT == 4) && KT_FA_ALT), "P·V split: 2 or 4 ranges, alternate tiles");
+  auto p_part = [&](int b, int i) { return bar0 + 8u * (R + 31 + 3 * b + i); };
   const uint32_t tmem_slot = bar0 + 8u * CF::NUM_BARS;
   const volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<const volatile uint32_t*>(base_ptr + CF::BAR_OFFSET + 8 * CF::NUM_BARS);
@@ -289,6 +301,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       mbar_init(s_free(s), (KT_FA_ALT ? SOFTMAX_WARPS / 2 : SOFTMAX_WARPS) * AW);
       mbar_init(p_full(s), (KT_FA_ALT ? SOFTMAX_WARPS / 2 : SOFTMAX_WARPS) * AW);
       mbar_init(o_done_of(s), 1);
+      for (int i = 0; i + 1 < PSPLIT; ++i) mbar_init(p_part(s, i), SOFTMAX_WARPS / 2 * AW);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(k_full(s), 1);
@@ -412,7 +425,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       };
       // O += P_t·V (O = P_t·V for the first tile of an item); needs P_t and the V tile
       auto pv_step = [&](int t, int k, bool first, bool last) -> bool {
-        if (!mbar_wait(p_full(sbuf(t)), sph(t))) return false;
+        if (!mbar_wait(PSPLIT > 1 ? p_part(sbuf(t), 0) : p_full(sbuf(t)), sph(t))) return false;
         if (!mbar_wait(v_full(vc % VSTAGES), (uint32_t)(vc / VSTAGES) & 1u)) return false;
         // the epilogue must have read the previous item's O before it is overwritten
         if (first && !mbar_wait(o_empty, ((uint32_t)k & 1u) ^ 1u)) return false;
@@ -424,6 +437,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         const uint32_t o_tmem = tmem + CF::COL_O;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
+          // key range r = kk / (8 / PSPLIT) starts once its P columns are stored
+          constexpr int PER = BN / 16 / PSPLIT;
+          if (PSPLIT > 1 && kk > 0 && kk % PER == 0) {
+            const int r = kk / PER;
+            if (!mbar_wait(r + 1 < PSPLIT ? p_part(sbuf(t), r) : p_full(sbuf(t)), sph(t))) return false;
+            tc_fence_after();
+          }
           // 16 keys per MMA: rows 16kk..16kk+15 of every 64-column V slab; slabs CF::SLAB apart
           // P over S from column halves: keys 64h.. at column 64h; otherwise keys in order
           const uint32_t p_col =
@@ -635,7 +655,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             float p0, p1;
             if (KT_FA_EXP16) {
               ex2_h2(x0, x1, p0, p1);
-            } else if (POLY && (i & 3) == 3) {
+            } else if (POLY && (i & 3) >= 4 - KT_FA_POLY) {
               p0 = ex2_poly(x0);
               p1 = ex2_poly(x1);
             } else {
@@ -658,6 +678,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             tmem_ld_wait();
             mask32(sc, c);
             sum += exp_chunk(sc, c, poly_tag);
+            // the P columns of a key range that is not the last: P·V may start on them
+            constexpr int CPR = BN / 32 / PSPLIT;  // 32-key chunks per range
+            if (PSPLIT > 1 && (c / 32 + 1) % CPR == 0 && c + 32 < BN) {
+              tmem_st_wait();
+              tc_fence_before();
+              warp_arrive(p_part(sbuf(t), (c / 32 + 1) / CPR - 1));
+            }
           }
           return sum;
         };
@@ -774,7 +801,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
               float p0, p1;
               if (KT_FA_EXP16) {
                 ex2_h2(x0, x1, p0, p1);
-              } else if (POLY && (i & 3) == 3) {
+              } else if (POLY && (i & 3) >= 4 - KT_FA_POLY) {
                 p0 = ex2_poly(x0);
                 p1 = ex2_poly(x1);
               } else {

@@ -136,15 +136,19 @@ def test_naive_attention_matches(dev, lib):
         assert ref.normwise_rel_err(got, oracle(inp["q"], inp["k"], inp["v"], inp["scale"], causal)) <= TOL
 
 
-@pytest.mark.parametrize("params", [{"kind": 2, "order": 0}, {"kind": 2, "order": 1},
-                                    {"kind": 1, "exp16": 1}, {"kind": 1, "poly_exp2": 1},
-                                    {"kind": 1, "alt": 1}, {"kind": 1, "alt": 1, "issuers": 1},
-                                    {"kind": 1, "alt": 0}, {"kind": 1, "sbuf": 3}, {"kind": 1, "sbuf": 2},
-                                    {"kind": 1, "sbuf": 3, "x2": 1, "poly_exp2": 1},
-                                    {"kind": 1, "warp_arrive": 1}, {"kind": 1, "warp_arrive": 1, "sbuf": 3},
-                                    {"kind": 1, "warp_arrive": 1, "alt": 1},
-                                    {"kind": 1, "sbuf": 3, "spec0": 1, "dephase": 600},
-                                    {"kind": 1, "sbuf": 3, "alt": 1}])
+@pytest.mark.parametrize("params", [
+    {"kind": 2, "order": 0}, {"kind": 2, "order": 1},
+    # column-half softmax (two warps per row), with its own axes
+    {"kind": 1, "alt": 0, "sbuf": 2}, {"kind": 1, "alt": 0, "sbuf": 3}, {"kind": 1, "alt": 0, "exp16": 1},
+    {"kind": 1, "alt": 0, "poly_exp2": 1, "x2": 0}, {"kind": 1, "alt": 0, "sbuf": 3, "x2": 1, "poly_exp2": 1},
+    {"kind": 1, "alt": 0, "warp_arrive": 1}, {"kind": 1, "alt": 0, "warp_arrive": 1, "sbuf": 3},
+    {"kind": 1, "alt": 0, "sbuf": 3, "spec0": 1, "dephase": 600}, {"kind": 1, "alt": 0, "issuers": 1},
+    # alternate-tile softmax (one warp per row and tile)
+    {"kind": 1, "alt": 1, "sbuf": 2, "psplit": 1, "x2": 0, "poly_exp2": 0}, {"kind": 1, "alt": 1, "issuers": 1},
+    {"kind": 1, "alt": 1, "sbuf": 3, "psplit": 1}, {"kind": 1, "alt": 1, "exp16": 1},
+    {"kind": 1, "alt": 1, "psplit": 4}, {"kind": 1, "alt": 1, "sbuf": 2, "psplit": 2},
+    {"kind": 1, "alt": 1, "poly_exp2": 2}, {"kind": 1, "alt": 1, "warp_arrive": 1},
+])
 def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
     """Kernels of the tuner's attention axes, built as variant libraries: the
     two-query-tile ping-pong kernel (both MMA issue orders), the half-precision /
