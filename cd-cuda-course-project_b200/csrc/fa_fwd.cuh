@@ -57,10 +57,13 @@
 #define KT_FA_ALT 1  // 1: the two softmax warps of a TMEM lane quarter take alternate S tiles, whole 128-key
                      // rows (their latency phases overlap the other warp's exponentials); 0: column halves
 #endif
+#ifndef KT_FA_BN
+#define KT_FA_BN 128  // keys per S tile: 128, or 96 (alternate-tile softmax; four S buffers fit TMEM)
+#endif
 #ifndef KT_FA_SBUF
 // S accumulators in TMEM: 2 (P in its own columns) or 3 (P written over its S tile; needs the two
 // issuers and scores that are not reloaded after P is written)
-#define KT_FA_SBUF ((KT_FA_ISSUERS == 2 && !KT_FA_RELOAD) ? 3 : 2)
+#define KT_FA_SBUF ((KT_FA_ISSUERS == 2 && !KT_FA_RELOAD) ? (KT_FA_BN == 96 ? 4 : 3) : 2)
 #endif
 #ifndef KT_FA_X2
 #define KT_FA_X2 1  // 1: the exponent arguments and row sums in packed fma.rn.f32x2 / add.rn.f32x2
@@ -70,7 +73,7 @@
 #endif
 #ifndef KT_FA_PSPLIT
 // alternate tiles: P_t·V issued in this many key ranges (1, 2 or 4), each once its P columns are stored
-#define KT_FA_PSPLIT (KT_FA_ALT ? 2 : 1)
+#define KT_FA_PSPLIT ((KT_FA_ALT && KT_FA_BN == 128) ? 2 : 1)
 #endif
 #ifndef KT_FA_SPEC0
 #define KT_FA_SPEC0 0  // 1: an item's first tile also speculates, on the previous item's final running max
@@ -93,7 +96,8 @@ namespace kt {
 namespace fa {
 
 constexpr int BM = 128;
-constexpr int BN = 128;  // keys per tile (the S accumulator is 128 columns)
+constexpr int BN = KT_FA_BN;  // keys per tile (the S accumulator is BN fp32 columns)
+static_assert(BN == 128 || (BN == 96 && KT_FA_ALT), "96-key tiles: alternate-tile softmax only");
 constexpr int SOFTMAX_WARPS = 8;
 constexpr int V_LOADER_WARP = 2 + SOFTMAX_WARPS;
 constexpr int EPI_THREADS = 128;  // warps 11-14: one query row per thread
@@ -110,7 +114,8 @@ struct Cfg {
   static constexpr int REGIONS = D / 64;            // 128-byte (64 bf16) column slabs per row
   static constexpr int SLAB = 128 * 128;            // one slab of 128 rows × 128 bytes
   static constexpr int Q_BYTES = REGIONS * SLAB;    // 128 rows × D bf16
-  static constexpr int K_BYTES = REGIONS * SLAB;    // BN keys × D
+  static constexpr int K_BYTES = REGIONS * SLAB;    // slot of up to 128 keys × D (slabs SLAB apart)
+  static constexpr int KV_TX = REGIONS * BN * 128;  // bytes one K or V tile of BN keys delivers
   static constexpr int V_BYTES = REGIONS * SLAB;
   static constexpr int Q_OFFSET = 0;                // two Q buffers: the next item's tile loads early
   static constexpr int K_OFFSET = 2 * Q_BYTES;
@@ -120,18 +125,19 @@ struct Cfg {
   // [2 item parity][2 parity][128] the maxima they are relative to
   static constexpr int RED_OFFSET = V_OFFSET + VSTAGES * V_BYTES;
   static constexpr int BAR_OFFSET = RED_OFFSET + 10 * 128 * 4;
-  // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[3], s_free[3],
-  // p_full[3], l_full[2], l_empty[2], o_done[3], o_final, o_empty, done, pair[4], decision[4][2],
-  // p_part[3][3]
-  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 31 + 9;
+  // q_full[2], q_empty[2], k_full[S], k_empty[S], v_full[VS], v_empty[VS], s_full[4], s_free[4],
+  // p_full[4], l_full[2], l_empty[2], o_done[4], o_final, o_empty, done, pair[4], decision[4][2],
+  // p_part[4][3]
+  static constexpr int NUM_BARS = 4 + 2 * STAGES + 2 * VSTAGES + 35 + 12;
   static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
   static constexpr uint32_t TMEM_COLS = 512;
-  // S buffers from column 0 (128 columns each), then O; with two S buffers P has its own
-  // 2 x 64 columns, with three each P_t (bf16 pairs) overwrites the first half of its S half
+  // S buffers from column 0 (BN columns each), then O; with two S buffers P has its own
+  // 2 x 64 columns, with three or four each P_t (bf16 pairs) is written over its S tile
   static constexpr int NB = KT_FA_SBUF;
-  static_assert(NB == 2 || NB == 3, "S buffers");
-  static constexpr uint32_t COL_S = 0, COL_O = NB * 128, COL_P = 384;
+  static_assert(NB == 2 || NB == 3 || NB == 4, "S buffers");
+  static_assert(NB * BN + D <= 512 && (NB > 2 || BN == 128), "TMEM columns");
+  static constexpr uint32_t COL_S = 0, COL_O = NB * BN, COL_P = 384;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -189,6 +195,40 @@ __device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1) {
   asm("add.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(a));
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
 }
+// 2^x0, 2^x1 as ex2_poly with the floating-point steps on packed fp32 pairs (five
+// instructions per pair instead of ten) and the exponent insertion as one shift-add
+// per value: (bits(y) - bits(1.5·2^23)) << 23 equals bits(y) << 23 modulo 2^32.
+__device__ __forceinline__ void ex2_poly_x2(float x0, float x1, float& p0, float& p1) {
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  uint64_t x, y, n, f, p, c, nc, a3, a2, a1, a0;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(x0), "f"(x1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(c) : "f"(12582912.0f));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(nc) : "f"(-12582912.0f));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(a3) : "f"(0.055029310286045074f));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(a2) : "f"(0.2422567903995514f));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(a1) : "f"(0.6932530403137207f));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(a0) : "f"(0.9999513626098633f));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(y) : "l"(x), "l"(c));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(n) : "l"(y), "l"(nc));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(f) : "l"(x), "l"(n));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(a3), "l"(f), "l"(a2));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(p), "l"(f), "l"(a1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(p) : "l"(p), "l"(f), "l"(a0));
+  uint32_t pl, ph, yl, yh;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(pl), "=r"(ph) : "l"(p));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(yl), "=r"(yh) : "l"(y));
+  p0 = __uint_as_float(pl + (yl << 23));
+  p1 = __uint_as_float(ph + (yh << 23));
+}
+
+// max of three fp32 values in one instruction
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -247,27 +287,28 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   static_assert(NB == 2 || (KT_FA_ISSUERS == 2 && !KT_FA_RELOAD),
                 "P over S: two issuers, scores not reloaded after P is written");
   // tile t uses S buffer sbuf(t); sph(t) is the phase parity of that buffer's barriers for tile t
-  auto sbuf = [](int t) { return NB == 2 ? (t & 1) : t % NB; };
-  auto sph = [](int t) { return (uint32_t)((NB == 2 ? (t >> 1) : t / NB) & 1); };
+  auto sbuf = [](int t) { return NB == 3 ? t % 3 : (t & (NB - 1)); };
+  auto sph = [](int t) { return (uint32_t)((NB == 3 ? t / 3 : (t >> (NB == 4 ? 2 : 1))) & 1); };
   auto s_full = [&](int b) { return bar0 + 8u * (R + b); };
-  auto s_free = [&](int b) { return bar0 + 8u * (R + 3 + b); };
-  auto p_full = [&](int b) { return bar0 + 8u * (R + 6 + b); };
-  auto l_full = [&](int b) { return bar0 + 8u * (R + 9 + b); };
-  auto l_empty = [&](int b) { return bar0 + 8u * (R + 11 + b); };
-  const uint32_t o_done = bar0 + 8u * (R + 13);  // one issuer: one phase per P·V product
+  auto s_free = [&](int b) { return bar0 + 8u * (R + 4 + b); };
+  auto p_full = [&](int b) { return bar0 + 8u * (R + 8 + b); };
+  auto l_full = [&](int b) { return bar0 + 8u * (R + 12 + b); };
+  auto l_empty = [&](int b) { return bar0 + 8u * (R + 14 + b); };
+  const uint32_t o_done = bar0 + 8u * (R + 16);  // one issuer: one phase per P·V product
   // two issuers: o_done_of(t) completes once per P_t·V of the tiles using S buffer sbuf(t)
-  auto o_done_of = [&](int t) { return bar0 + 8u * (R + 13 + sbuf(t)); };
-  const uint32_t o_final = bar0 + 8u * (R + 16);  // one phase per item: its last P·V product landed
-  const uint32_t o_empty = bar0 + 8u * (R + 17);  // one phase per item: the epilogue has read O
-  const uint32_t done_bar = bar0 + 8u * (R + 18);
-  const uint32_t pair_bar0 = bar0 + 8u * (R + 19);  // 4 softmax warp-pair exchanges
+  auto o_done_of = [&](int t) { return bar0 + 8u * (R + 16 + sbuf(t)); };
+  const uint32_t o_final = bar0 + 8u * (R + 20);  // one phase per item: its last P·V product landed
+  const uint32_t o_empty = bar0 + 8u * (R + 21);  // one phase per item: the epilogue has read O
+  const uint32_t done_bar = bar0 + 8u * (R + 22);
+  const uint32_t pair_bar0 = bar0 + 8u * (R + 23);  // 4 softmax warp-pair exchanges
   // alternate tiles: the running-max decision of tile parity p for lane quarter q
-  auto dec_bar = [&](int q, int p) { return bar0 + 8u * (R + 23 + 2 * q + p); };
+  auto dec_bar = [&](int q, int p) { return bar0 + 8u * (R + 27 + 2 * q + p); };
   // alternate tiles, P·V in KT_FA_PSPLIT key ranges: range i < KT_FA_PSPLIT-1 of buffer b is
   // stored (the last range is signalled by p_full)
   constexpr int PSPLIT = KT_FA_PSPLIT;
-  static_assert(PSPLIT == 1 || ((PSPLIT == 2 || PSPLIT == 4) && KT_FA_ALT), "P·V split: 2 or 4 ranges, alternate tiles");
-  auto p_part = [&](int b, int i) { return bar0 + 8u * (R + 31 + 3 * b + i); };
+  static_assert(PSPLIT == 1 || (KT_FA_ALT && PSPLIT <= 4 && (BN / 32) % PSPLIT == 0),
+                "P·V split: ranges of whole 32-key chunks, alternate tiles");
+  auto p_part = [&](int b, int i) { return bar0 + 8u * (R + 35 + 3 * b + i); };
   const uint32_t tmem_slot = bar0 + 8u * CF::NUM_BARS;
   const volatile uint32_t* tmem_slot_ptr =
       reinterpret_cast<const volatile uint32_t*>(base_ptr + CF::BAR_OFFSET + 8 * CF::NUM_BARS);
@@ -376,7 +417,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             break;
           }
           const uint32_t dst = base + (is_k ? CF::K_OFFSET + s * CF::K_BYTES : CF::V_OFFSET + s * CF::V_BYTES);
-          mbar_arrive_expect_tx(full, CF::K_BYTES);
+          mbar_arrive_expect_tx(full, CF::KV_TX);
 #pragma unroll
           for (int r = 0; r < CF::REGIONS; ++r)
             tma_load_3d(dst + r * CF::SLAB, is_k ? &tm_k : &tm_v, 64 * r, j * BN, bh, full);
@@ -585,7 +626,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // row maximum over the 128 keys, two 32-column loads in flight at a time
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < BN; c += 64) {
+        for (int c = 0; c + 64 <= BN; c += 64) {
           uint32_t va[32], vb[32];
           tmem_ld32(s_addr + (uint32_t)c, va);
           tmem_ld32(s_addr + (uint32_t)(c + 32), vb);
@@ -594,7 +635,18 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           mask32(vb, c + 32);
           float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-          for (int i = 0; i < 32; ++i) m4[i & 3] = fmaxf(m4[i & 3], fmaxf(__uint_as_float(va[i]), __uint_as_float(vb[i])));
+          for (int i = 0; i < 32; ++i) m4[i & 3] = fmax3f(m4[i & 3], __uint_as_float(va[i]), __uint_as_float(vb[i]));
+          mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        }
+        if constexpr (BN % 64 == 32) {  // the last 32 keys of a 96-key tile
+          uint32_t va[32];
+          tmem_ld32(s_addr + (uint32_t)(BN - 32), va);
+          tmem_ld_wait();
+          mask32(va, BN - 32);
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            m4[(i >> 1) & 3] = fmax3f(m4[(i >> 1) & 3], __uint_as_float(va[i]), __uint_as_float(va[i + 1]));
           mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
         }
         const float m_tile = mx * scale_log2;
@@ -656,8 +708,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             if (KT_FA_EXP16) {
               ex2_h2(x0, x1, p0, p1);
             } else if (POLY && (i & 3) >= 4 - KT_FA_POLY) {
-              p0 = ex2_poly(x0);
-              p1 = ex2_poly(x1);
+              if (KT_FA_X2) {
+                ex2_poly_x2(x0, x1, p0, p1);
+              } else {
+                p0 = ex2_poly(x0);
+                p1 = ex2_poly(x1);
+              }
             } else {
               p0 = ex2(x0);
               p1 = ex2(x1);
@@ -706,6 +762,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       warp_arrive(l_full(lb));
     }
   } else if (warp < V_LOADER_WARP) {
+#if KT_FA_BN == 128  // the column-half split needs 64-key halves
     // softmax: TMEM lane quarter = warp % 4, the two warps of a quarter split the columns
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
@@ -802,8 +859,12 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
               if (KT_FA_EXP16) {
                 ex2_h2(x0, x1, p0, p1);
               } else if (POLY && (i & 3) >= 4 - KT_FA_POLY) {
-                p0 = ex2_poly(x0);
-                p1 = ex2_poly(x1);
+                if (KT_FA_X2) {
+                  ex2_poly_x2(x0, x1, p0, p1);
+                } else {
+                  p0 = ex2_poly(x0);
+                  p1 = ex2_poly(x1);
+                }
               } else {
                 p0 = ex2(x0);
                 p1 = ex2(x1);
@@ -912,6 +973,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       warp_arrive(l_full(lb));
       m_guess = m_run;
     }
+#endif
   } else {
     // epilogue warps: O / l -> bf16, one query row per thread; O is released to the
     // next item's first P·V product as soon as it is in registers
@@ -971,13 +1033,13 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   }
 }
 
-// [B·H, S, D] bf16 viewed as a 3-D tensor (D, S, B·H); box 64 × 128 × 1, 128-byte swizzle.
-inline int make_tmap_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S, int64_t D) {
+// [B·H, S, D] bf16 viewed as a 3-D tensor (D, S, B·H); box 64 × rows × 1, 128-byte swizzle.
+inline int make_tmap_bhsd(CUtensorMap* map, const void* base, int64_t BH, int64_t S, int64_t D, uint32_t rows = 128) {
   PFN_encodeTiled enc = get_encode_tiled();
   if (enc == nullptr) return fail(KT_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
   cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -991,9 +1053,9 @@ inline int launch_t(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uin
                     float scale, cudaStream_t st) {
   using CF = Cfg<D, KT_FA_STAGES, KT_FA_VSTAGES>;
   CUtensorMap tq, tk, tv;
-  int rc = make_tmap_bhsd(&tq, Q, BH, S, D);
-  if (rc == KT_OK) rc = make_tmap_bhsd(&tk, K, BH, S, D);
-  if (rc == KT_OK) rc = make_tmap_bhsd(&tv, V, BH, S, D);
+  int rc = make_tmap_bhsd(&tq, Q, BH, S, D, BM);
+  if (rc == KT_OK) rc = make_tmap_bhsd(&tk, K, BH, S, D, BN);  // K and V tiles of BN keys
+  if (rc == KT_OK) rc = make_tmap_bhsd(&tv, V, BH, S, D, BN);
   if (rc != KT_OK) return rc;
   auto kern = fa_fwd_kernel<D, KT_FA_STAGES, CAUSAL>;
   rc = ensure_smem((const void*)kern, CF::SMEM_BYTES, "attention: smem attribute");

@@ -231,12 +231,13 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["poly_exp2"] = [0, 1, 2]    # kind 1: n of every 4 exponential pairs on the FMA pipe (polynomial)
         space["issuers"] = [1, 2]         # kind 1: threads issuing tcgen05.mma (2: S and P·V from two warps)
         space["alt"] = [0, 1]             # kind 1: softmax warps of a lane quarter take alternate S tiles (1)
-        space["sbuf"] = [2, 3]            # kind 1: S accumulators in TMEM (3: P written over its S tile)
+        space["sbuf"] = [2, 3, 4]         # kind 1: S accumulators in TMEM (3, 4: P written over its S tile)
         space["x2"] = [0, 1]              # kind 1: exponent arguments and row sums in packed f32x2 instructions
         space["warp_arrive"] = [0, 1]     # kind 1: one mbarrier arrival per warp instead of per thread
         space["spec0"] = [0, 1]           # kind 1: first tile of an item speculates on the previous item's max
         space["dephase"] = [0, 400, 800]  # kind 1: clocks the second softmax warp of a scheduler starts late
-        space["psplit"] = [1, 2, 4]       # kind 1, alternate tiles: P·V issued per key range as P is stored
+        space["psplit"] = [1, 2, 3, 4]    # kind 1, alternate tiles: P·V issued per key range as P is stored
+        space["bn"] = [128, 96]           # kind 1: keys per S tile (96: four S buffers in TMEM)
         space["order"] = [0, 1]           # kind 2: MMA issue order (0 ping-pong, 1 in phase)
         space["poly_every"] = [0, 4, 8]   # kind 2: every n-th exponential pair on the FMA pipe (0: none)
         space["causal"] = [False, True]
@@ -300,15 +301,23 @@ def is_valid(kernel: str, params: dict) -> bool:
             return (params.get("stages", 2), params.get("v_stages", 2), params.get("poly_exp2", 0),
                     params.get("issuers", 2), params.get("alt", 0), params.get("sbuf", 2), params.get("x2", 0),
                     params.get("warp_arrive", 0), params.get("spec0", 0),
-                    params.get("dephase", 0), params.get("psplit", 1)) == (2, 2, 0, 2, 0, 2, 0, 0, 0, 0, 1)
+                    params.get("dephase", 0), params.get("psplit", 1),
+                    params.get("bn", 128)) == (2, 2, 0, 2, 0, 2, 0, 0, 0, 0, 1, 128)
         if params.get("order", 0) != 0 or params.get("poly_every", 0) != 0:
             return False
         if params.get("alt", 0) and (params.get("spec", 1) != 1 or params.get("reload", 0) != 0
                                      or params.get("spec0", 0) or params.get("dephase", 0)):
             return False  # whole-row softmax: the column-half exchange axes do not shape it
+        bn = params.get("bn", 128)
+        if (bn // 32) % params.get("psplit", 1):
+            return False  # P·V key ranges are whole 32-key chunks
+        if bn == 96 and (not params.get("alt", 0) or params.get("issuers", 2) != 2 or params.get("sbuf", 4) != 4):
+            return False  # 96-key tiles: four S buffers, alternate-tile softmax, two issuers
+        if bn == 128 and params.get("sbuf", 2) == 4:
+            return False  # four 128-key S buffers leave no TMEM columns for O
         if params.get("psplit", 1) != 1 and not params.get("alt", 0):
             return False  # the split P·V issue follows the whole-row P stores of the alternate-tile softmax
-        if params.get("sbuf", 2) == 3 and (params.get("issuers", 2) != 2 or params.get("reload", 0)):
+        if params.get("sbuf", 2) >= 3 and (params.get("issuers", 2) != 2 or params.get("reload", 0)):
             return False  # P over S needs the two issuers and the scores kept in registers
         # head dim 128: two Q buffers + (K + V slots) x 32 KB must fit the 227 KB of shared memory
         return params.get("stages", 2) + params.get("v_stages", 2) <= 4

@@ -148,13 +148,16 @@ def test_naive_attention_matches(dev, lib):
     {"kind": 1, "alt": 1, "sbuf": 3, "psplit": 1}, {"kind": 1, "alt": 1, "exp16": 1},
     {"kind": 1, "alt": 1, "psplit": 4}, {"kind": 1, "alt": 1, "sbuf": 2, "psplit": 2},
     {"kind": 1, "alt": 1, "poly_exp2": 2}, {"kind": 1, "alt": 1, "warp_arrive": 1},
+    # 96-key tiles, four S buffers
+    {"kind": 1, "alt": 1, "bn": 96}, {"kind": 1, "alt": 1, "bn": 96, "psplit": 3},
 ])
 def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
     """Kernels of the tuner's attention axes, built as variant libraries: the
     two-query-tile ping-pong kernel (both MMA issue orders), the half-precision /
     polynomial exponentials, both softmax splits (column halves, alternate
-    tiles) and two or three S buffers in TMEM (P in its own columns or over its
-    S tile), against the oracle, including scores whose running max rises."""
+    tiles), two to four S buffers in TMEM (P in its own columns or over its S
+    tile) and 96-key tiles (partial last tiles at every sequence length here),
+    against the oracle, including scores whose running max rises."""
     monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
     import generator
     ok, log, so = generator.ensure_variant("attention", params)
