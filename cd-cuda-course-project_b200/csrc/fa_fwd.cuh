@@ -75,6 +75,9 @@
 // alternate tiles: P_t·V issued in this many key ranges (1, 2 or 4), each once its P columns are stored
 #define KT_FA_PSPLIT ((KT_FA_ALT && KT_FA_BN == 128) ? 2 : 1)
 #endif
+#ifndef KT_FA_FUSE
+#define KT_FA_FUSE 0  // 1: alternate tiles, one speculative pass over the scores per tile (max checked per chunk)
+#endif
 #ifndef KT_FA_SPEC0
 #define KT_FA_SPEC0 0  // 1: an item's first tile also speculates, on the previous item's final running max
 #endif
@@ -596,16 +599,29 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
       const int n_kv = kv_tiles<CAUSAL>(qt, S);
       const int q0 = qt * BM;
       const int qrow = q0 + row;
-      float my_m = -INFINITY;  // the maximum l_part is relative to
+      float my_m = -INFINITY;    // the maximum l_part is relative to
+      float my_dec = -INFINITY;  // this warp's decision for its previous tile of this item
       float l_part = 0.f;
       for (int j = 0; j < n_kv; ++j, ++t) {
         if ((t & 1) != h) continue;
-        // the decision of tile t-1 (made by the other parity's warp of this quarter)
-        if (t > 0 && !__all_sync(0xffffffffu, mbar_wait(dec_bar(quarter, (t - 1) & 1), (uint32_t)((t - 1) >> 1) & 1u))) {
-          timed_out = true;
-          break;
+        const uint32_t dec_prev = dec_bar(quarter, (t - 1) & 1);
+        const uint32_t dec_prev_ph = (uint32_t)((t - 1) >> 1) & 1u;
+        // Fused speculative pass (KT_FA_FUSE, from this warp's second tile of the item
+        // on): one pass over the scores with the newest running max this warp knows,
+        // checked against the exact decision of tile t-1 at the end. Otherwise two
+        // passes: the row max first, then the exponentials with the decided max.
+        const bool fuse = KT_FA_FUSE && j >= 2;
+        bool known = true;
+        if (!fuse) {
+          // the decision of tile t-1 (made by the other parity's warp of this quarter)
+          if (t > 0 && !__all_sync(0xffffffffu, mbar_wait(dec_prev, dec_prev_ph))) {
+            timed_out = true;
+            break;
+          }
+        } else {
+          known = __all_sync(0xffffffffu, mbar_try_wait(dec_prev, dec_prev_ph));
         }
-        const float m_prev = (j == 0) ? -INFINITY : m_sh[(k & 1) * 128 + row];
+        float m_prev = (j == 0) ? -INFINITY : (known ? m_sh[(k & 1) * 128 + row] : my_dec);
         if (!__all_sync(0xffffffffu, mbar_wait(s_full(sbuf(t)), sph(t)))) {
           timed_out = true;
           break;
@@ -623,75 +639,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             }
           }
         };
-        // row maximum over the 128 keys, two 32-column loads in flight at a time
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c + 64 <= BN; c += 64) {
-          uint32_t va[32], vb[32];
-          tmem_ld32(s_addr + (uint32_t)c, va);
-          tmem_ld32(s_addr + (uint32_t)(c + 32), vb);
-          tmem_ld_wait();
-          mask32(va, c);
-          mask32(vb, c + 32);
-          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-          for (int i = 0; i < 32; ++i) m4[i & 3] = fmax3f(m4[i & 3], __uint_as_float(va[i]), __uint_as_float(vb[i]));
-          mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-        }
-        if constexpr (BN % 64 == 32) {  // the last 32 keys of a 96-key tile
-          uint32_t va[32];
-          tmem_ld32(s_addr + (uint32_t)(BN - 32), va);
-          tmem_ld_wait();
-          mask32(va, BN - 32);
-          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            m4[(i >> 1) & 3] = fmax3f(m4[(i >> 1) & 3], __uint_as_float(va[i]), __uint_as_float(va[i + 1]));
-          mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-        }
-        const float m_tile = mx * scale_log2;
-        const bool raise = m_tile > m_prev + kRescaleThreshold;
-        const float m_new = raise ? m_tile : m_prev;
-        m_sh[(k & 1) * 128 + row] = m_new;
-        warp_arrive(dec_bar(quarter, t & 1));  // release: m_sh is visible to the waiting warp
-        // O holds P_0..P_{j-1}·V of this item under m_prev: rescale the raised rows
-        if (j > 0 && __any_sync(0xffffffffu, raise)) {
-          const float alpha = raise ? ((m_prev == -INFINITY) ? 0.f : ex2(m_prev - m_new)) : 1.f;
-          const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), sph(t - 1))
-                                                  : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
-          if (!__all_sync(0xffffffffu, o_ready)) {
-            timed_out = true;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < HD4; c += 32) {
-            uint32_t v[32];
-            const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)c;
-            tmem_ld32(oa, v);
-            tmem_ld_wait();
-            uint32_t w0[16], w1[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              w0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-              w1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
-            }
-            tmem_st16(oa, w0);
-            tmem_st16(oa + 16u, w1);
-          }
-          tmem_st_wait();
-        }
-        // this warp's row-sum share follows the maximum
-        if (my_m != m_new) {
-          l_part = (my_m == -INFINITY) ? 0.f : l_part * ex2(my_m - m_new);
-          my_m = m_new;
-        }
-        // p = 2^(s·c − m_new) into P buffer h (bf16, 64 columns); scores reloaded 32 columns at a time,
-        // the next chunk's load in flight while the current one is exponentiated
         // P: 64 columns of its own, or over the scores (chunk c's P lands in columns c/2..c/2+15,
         // all of them already read)
         const uint32_t p_addr = NB == 2 ? tmem + lane_off + CF::COL_P + (uint32_t)(h * 64) : s_addr;
-        auto exp_chunk = [&](const uint32_t (&sc)[32], int c, auto poly_tag) -> float {
+        // p = 2^(s·c − m) for one 32-key chunk into P (bf16); returns the chunk's sum
+        auto exp_chunk = [&](const uint32_t (&sc)[32], int c, float m, auto poly_tag) -> float {
           constexpr bool POLY = decltype(poly_tag)::value;
           float s4[4] = {0.f, 0.f, 0.f, 0.f};
           uint32_t pk[16];
@@ -699,10 +651,10 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           for (int i = 0; i < 16; ++i) {
             float x0, x1;
             if (KT_FA_X2) {
-              fma2_bc(x0, x1, __uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), scale_log2, -m_new);
+              fma2_bc(x0, x1, __uint_as_float(sc[2 * i]), __uint_as_float(sc[2 * i + 1]), scale_log2, -m);
             } else {
-              x0 = fmaf(__uint_as_float(sc[2 * i]), scale_log2, -m_new);
-              x1 = fmaf(__uint_as_float(sc[2 * i + 1]), scale_log2, -m_new);
+              x0 = fmaf(__uint_as_float(sc[2 * i]), scale_log2, -m);
+              x1 = fmaf(__uint_as_float(sc[2 * i + 1]), scale_log2, -m);
             }
             float p0, p1;
             if (KT_FA_EXP16) {
@@ -725,28 +677,168 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           tmem_st16(p_addr + (uint32_t)(c / 2), pk);
           return (s4[0] + s4[1]) + (s4[2] + s4[3]);
         };
-        auto exp_row = [&](auto poly_tag) -> float {
-          float sum = 0.f;
+        // multiply the first `cols` columns of stored P (bf16 pairs) of this row by f
+        auto rescale_p = [&](int cols, float f) {
+          tmem_st_wait();
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t sc[32];
-            tmem_ld32(s_addr + (uint32_t)c, sc);
+          for (int cc = 0; cc < cols; cc += 16) {
+            uint32_t v[16];
+            tmem_ld16(p_addr + (uint32_t)cc, v);
             tmem_ld_wait();
-            mask32(sc, c);
-            sum += exp_chunk(sc, c, poly_tag);
-            // the P columns of a key range that is not the last: P·V may start on them
-            constexpr int CPR = BN / 32 / PSPLIT;  // 32-key chunks per range
-            if (PSPLIT > 1 && (c / 32 + 1) % CPR == 0 && c + 32 < BN) {
-              tmem_st_wait();
-              tc_fence_before();
-              warp_arrive(p_part(sbuf(t), (c / 32 + 1) / CPR - 1));
-            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              v[i] = pack_bf16(__uint_as_float(v[i] << 16) * f, __uint_as_float(v[i] & 0xffff0000u) * f);
+            tmem_st16(p_addr + (uint32_t)cc, v);
           }
-          return sum;
         };
-        l_part += (KT_FA_POLY && !mask_tile) ? exp_row(std::true_type{}) : exp_row(std::false_type{});
+        // O holds P_0..P_{j-1}·V of this item relative to m_from: rescale the raised rows
+        auto rescale_o = [&](bool raise, float m_from, float m_to) -> bool {
+          const float alpha = raise ? ((m_from == -INFINITY) ? 0.f : ex2(m_from - m_to)) : 1.f;
+          const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), sph(t - 1))
+                                                  : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
+          if (!__all_sync(0xffffffffu, o_ready)) return false;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < HD4; c += 32) {
+            uint32_t v[32];
+            const uint32_t oa = tmem + lane_off + CF::COL_O + (uint32_t)c;
+            tmem_ld32(oa, v);
+            tmem_ld_wait();
+            uint32_t w0[16], w1[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              w0[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+              w1[i] = __float_as_uint(__uint_as_float(v[16 + i]) * alpha);
+            }
+            tmem_st16(oa, w0);
+            tmem_st16(oa + 16u, w1);
+          }
+          tmem_st_wait();
+          return true;
+        };
+        float m_new, tile_sum;
+        if (!fuse) {
+          // row maximum over the tile, two 32-column loads in flight at a time
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c + 64 <= BN; c += 64) {
+            uint32_t va[32], vb[32];
+            tmem_ld32(s_addr + (uint32_t)c, va);
+            tmem_ld32(s_addr + (uint32_t)(c + 32), vb);
+            tmem_ld_wait();
+            mask32(va, c);
+            mask32(vb, c + 32);
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < 32; ++i) m4[i & 3] = fmax3f(m4[i & 3], __uint_as_float(va[i]), __uint_as_float(vb[i]));
+            mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+          }
+          if constexpr (BN % 64 == 32) {  // the last 32 keys of a 96-key tile
+            uint32_t va[32];
+            tmem_ld32(s_addr + (uint32_t)(BN - 32), va);
+            tmem_ld_wait();
+            mask32(va, BN - 32);
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int i = 0; i < 32; i += 2)
+              m4[(i >> 1) & 3] = fmax3f(m4[(i >> 1) & 3], __uint_as_float(va[i]), __uint_as_float(va[i + 1]));
+            mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+          }
+          const float m_tile = mx * scale_log2;
+          const bool raise = m_tile > m_prev + kRescaleThreshold;
+          m_new = raise ? m_tile : m_prev;
+          m_sh[(k & 1) * 128 + row] = m_new;
+          warp_arrive(dec_bar(quarter, t & 1));  // release: m_sh is visible to the waiting warp
+          if (j > 0 && __any_sync(0xffffffffu, raise) && !rescale_o(raise, m_prev, m_new)) {
+            timed_out = true;
+            break;
+          }
+          // scores reloaded 32 columns at a time, P written as each chunk is done
+          auto exp_row = [&](auto poly_tag) -> float {
+            float sum = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+              uint32_t sc[32];
+              tmem_ld32(s_addr + (uint32_t)c, sc);
+              tmem_ld_wait();
+              mask32(sc, c);
+              sum += exp_chunk(sc, c, m_new, poly_tag);
+              // the P columns of a key range that is not the last: P·V may start on them
+              constexpr int CPR = BN / 32 / PSPLIT;  // 32-key chunks per range
+              if (PSPLIT > 1 && (c / 32 + 1) % CPR == 0 && c + 32 < BN) {
+                tmem_st_wait();
+                tc_fence_before();
+                warp_arrive(p_part(sbuf(t), (c / 32 + 1) / CPR - 1));
+              }
+            }
+            return sum;
+          };
+          tile_sum = (KT_FA_POLY && !mask_tile) ? exp_row(std::true_type{}) : exp_row(std::false_type{});
+        } else {
+          // one pass: each chunk's maximum is checked against the max in use; rows
+          // whose scores pass it by more than the rescale threshold switch to the
+          // tile's running max (their stored P and sum are scaled down to it)
+          float m_use = m_prev, mt = -INFINITY, sum = 0.f;
+          auto pass = [&](auto poly_tag) {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+              uint32_t sc[32];
+              tmem_ld32(s_addr + (uint32_t)c, sc);
+              tmem_ld_wait();
+              mask32(sc, c);
+              float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+              for (int i = 0; i < 32; i += 2)
+                m4[(i >> 1) & 3] = fmax3f(m4[(i >> 1) & 3], __uint_as_float(sc[i]), __uint_as_float(sc[i + 1]));
+              const float cm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale_log2;
+              mt = fmaxf(mt, cm);
+              const bool bad = cm > m_use + kRescaleThreshold;
+              if (__any_sync(0xffffffffu, bad)) {
+                const float f = bad ? ex2(m_use - mt) : 1.f;
+                if (c > 0) rescale_p(c / 2, f);
+                sum *= f;
+                if (bad) m_use = mt;
+              }
+              sum += exp_chunk(sc, c, m_use, poly_tag);
+            }
+          };
+          if (KT_FA_POLY && !mask_tile) pass(std::true_type{});
+          else pass(std::false_type{});
+          // the exact decision of tile t-1, then this tile's
+          if (!known && !__all_sync(0xffffffffu, mbar_wait(dec_prev, dec_prev_ph))) {
+            timed_out = true;
+            break;
+          }
+          m_prev = m_sh[(k & 1) * 128 + row];
+          const bool raise = mt > m_prev + kRescaleThreshold;
+          m_new = raise ? mt : m_prev;
+          m_sh[(k & 1) * 128 + row] = m_new;
+          warp_arrive(dec_bar(quarter, t & 1));  // release: m_sh is visible to the waiting warp
+          // P relative to the decided max (rare: a raise in the other warp's tile or a switch here)
+          if (__any_sync(0xffffffffu, m_use != m_new)) {
+            const float f = (m_use != m_new) ? ex2(m_use - m_new) : 1.f;
+            rescale_p(BN / 2, f);
+            sum *= f;
+          }
+          if (__any_sync(0xffffffffu, raise) && !rescale_o(raise, m_prev, m_new)) {
+            timed_out = true;
+            break;
+          }
+          tile_sum = sum;
+        }
+        // this warp's row-sum share follows the maximum
+        if (my_m != m_new) {
+          l_part = (my_m == -INFINITY) ? 0.f : l_part * ex2(my_m - m_new);
+          my_m = m_new;
+        }
+        l_part += tile_sum;
+        my_dec = m_new;
         tmem_st_wait();
         tc_fence_before();
+        if (fuse) {
+          // the split P·V ranges are signalled only now that P is final
+          for (int i = 0; i + 1 < PSPLIT; ++i) warp_arrive(p_part(sbuf(t), i));
+        }
         warp_arrive(s_free(sbuf(t)));
         warp_arrive(p_full(sbuf(t)));
       }

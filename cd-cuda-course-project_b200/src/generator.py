@@ -63,7 +63,7 @@ MACROS: dict[str, dict[str, str]] = {
                   "spec": "KT_FA_SPEC", "reload": "KT_FA_RELOAD", "issuers": "KT_FA_ISSUERS",
                   "alt": "KT_FA_ALT", "sbuf": "KT_FA_SBUF", "x2": "KT_FA_X2",
                   "warp_arrive": "KT_FA_WARP_ARRIVE", "spec0": "KT_FA_SPEC0", "dephase": "KT_FA_DEPHASE",
-                  "psplit": "KT_FA_PSPLIT", "bn": "KT_FA_BN"},
+                  "psplit": "KT_FA_PSPLIT", "bn": "KT_FA_BN", "fuse": "KT_FA_FUSE"},
 }
 ONLY = {"softmax": "KT_ONLY_SOFTMAX", "layernorm": "KT_ONLY_LAYERNORM", "reduction": "KT_ONLY_REDUCE",
         "matmul": "KT_ONLY_GEMM", "attention": "KT_ONLY_FA"}

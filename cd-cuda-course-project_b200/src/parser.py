@@ -238,6 +238,7 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["dephase"] = [0, 400, 800]  # kind 1: clocks the second softmax warp of a scheduler starts late
         space["psplit"] = [1, 2, 3, 4]    # kind 1, alternate tiles: P·V issued per key range as P is stored
         space["bn"] = [128, 96]           # kind 1: keys per S tile (96: four S buffers in TMEM)
+        space["fuse"] = [0, 1]            # kind 1, alternate tiles: one speculative pass per tile
         space["order"] = [0, 1]           # kind 2: MMA issue order (0 ping-pong, 1 in phase)
         space["poly_every"] = [0, 4, 8]   # kind 2: every n-th exponential pair on the FMA pipe (0: none)
         space["causal"] = [False, True]
@@ -302,7 +303,7 @@ def is_valid(kernel: str, params: dict) -> bool:
                     params.get("issuers", 2), params.get("alt", 0), params.get("sbuf", 2), params.get("x2", 0),
                     params.get("warp_arrive", 0), params.get("spec0", 0),
                     params.get("dephase", 0), params.get("psplit", 1),
-                    params.get("bn", 128)) == (2, 2, 0, 2, 0, 2, 0, 0, 0, 0, 1, 128)
+                    params.get("bn", 128), params.get("fuse", 0)) == (2, 2, 0, 2, 0, 2, 0, 0, 0, 0, 1, 128, 0)
         if params.get("order", 0) != 0 or params.get("poly_every", 0) != 0:
             return False
         if params.get("alt", 0) and (params.get("spec", 1) != 1 or params.get("reload", 0) != 0
@@ -315,6 +316,8 @@ def is_valid(kernel: str, params: dict) -> bool:
             return False  # 96-key tiles: four S buffers, alternate-tile softmax, two issuers
         if bn == 128 and params.get("sbuf", 2) == 4:
             return False  # four 128-key S buffers leave no TMEM columns for O
+        if params.get("fuse", 0) and not params.get("alt", 0):
+            return False  # the fused pass belongs to the alternate-tile softmax
         if params.get("psplit", 1) != 1 and not params.get("alt", 0):
             return False  # the split P·V issue follows the whole-row P stores of the alternate-tile softmax
         if params.get("sbuf", 2) >= 3 and (params.get("issuers", 2) != 2 or params.get("reload", 0)):

@@ -150,6 +150,9 @@ def test_naive_attention_matches(dev, lib):
     {"kind": 1, "alt": 1, "poly_exp2": 2}, {"kind": 1, "alt": 1, "warp_arrive": 1},
     # 96-key tiles, four S buffers
     {"kind": 1, "alt": 1, "bn": 96}, {"kind": 1, "alt": 1, "bn": 96, "psplit": 3},
+    # one speculative pass per tile
+    {"kind": 1, "alt": 1, "fuse": 1}, {"kind": 1, "alt": 1, "fuse": 1, "sbuf": 2, "psplit": 1},
+    {"kind": 1, "alt": 1, "fuse": 1, "bn": 96},
 ])
 def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
     """Kernels of the tuner's attention axes, built as variant libraries: the
