@@ -619,7 +619,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
             break;
           }
         } else {
-          known = __all_sync(0xffffffffu, mbar_try_wait(dec_prev, dec_prev_ph));
+          known = __all_sync(0xffffffffu, mbar_test_wait(dec_prev, dec_prev_ph));
         }
         float m_prev = (j == 0) ? -INFINITY : (known ? m_sh[(k & 1) * 128 + row] : my_dec);
         if (!__all_sync(0xffffffffu, mbar_wait(s_full(sbuf(t)), sph(t)))) {

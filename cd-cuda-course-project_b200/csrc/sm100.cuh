@@ -57,6 +57,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: has the phase with `parity` completed? (try_wait may
+// suspend the thread for a while when it has not; test_wait never does.)
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with `parity` has completed. Gives up after
 // KT_WAIT_LIMIT_NS of wall time and returns false (the caller records the
 // timeout in the device error word and unwinds); never spins forever.
