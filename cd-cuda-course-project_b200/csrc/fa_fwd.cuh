@@ -61,9 +61,9 @@
 #define KT_FA_BN 128  // keys per S tile: 128, or 96 (alternate-tile softmax; four S buffers fit TMEM)
 #endif
 #ifndef KT_FA_SBUF
-// S accumulators in TMEM: 2 (P in its own columns) or 3 (P written over its S tile; needs the two
-// issuers and scores that are not reloaded after P is written)
-#define KT_FA_SBUF ((KT_FA_ISSUERS == 2 && !KT_FA_RELOAD) ? (KT_FA_BN == 96 ? 4 : 3) : 2)
+// S accumulators in TMEM: 2 (P in its own columns), 3 or 4 (P written over its S tile; needs
+// scores that are not reloaded after P is written)
+#define KT_FA_SBUF (KT_FA_RELOAD ? 2 : (KT_FA_BN == 96 ? 4 : (KT_FA_ISSUERS == 2 ? 3 : 2)))
 #endif
 #ifndef KT_FA_X2
 #define KT_FA_X2 1  // 1: the exponent arguments and row sums in packed fma.rn.f32x2 / add.rn.f32x2
@@ -287,8 +287,9 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
   auto v_empty = [&](int s) { return bar0 + 8u * (4 + 2 * STAGES + VSTAGES + s); };
   constexpr int R = 4 + 2 * STAGES + 2 * VSTAGES;
   constexpr int NB = CF::NB;
-  static_assert(NB == 2 || (KT_FA_ISSUERS == 2 && !KT_FA_RELOAD),
-                "P over S: two issuers, scores not reloaded after P is written");
+  static_assert(NB == 2 || !KT_FA_RELOAD, "P over S: scores not reloaded after P is written");
+  // per-buffer P·V completion barriers (o_done_of): two issuers, or P over S
+  constexpr bool PER_BUF = KT_FA_ISSUERS == 2 || NB > 2;
   // tile t uses S buffer sbuf(t); sph(t) is the phase parity of that buffer's barriers for tile t
   auto sbuf = [](int t) { return NB == 3 ? t % 3 : (t & (NB - 1)); };
   auto sph = [](int t) { return (uint32_t)((NB == 3 ? t / 3 : (t >> (NB == 4 ? 2 : 1))) & 1); };
@@ -495,7 +496,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           mma_f16_ts_w(o_tmem, p_tmem + p_col, v_lo + (uint32_t)(kk * 16 * 128 / 16), v_hi, idesc_o,
                        (!first || kk > 0) ? 1u : 0u);
         }
-        mma_commit(KT_FA_ISSUERS == 2 ? o_done_of(t) : o_done);
+        mma_commit(PER_BUF ? o_done_of(t) : o_done);
         mma_commit(v_empty(vc % VSTAGES));
         if (last) mma_commit(o_final);
         ++vc;
@@ -550,9 +551,11 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           break;
         }
         for (int j = 0; j < n_kv; ++j, ++t) {
-          // K tile, and S buffer t&1 last read by the softmax of tile t-2
+          // K tile, and S buffer sbuf(t) last read by the softmax of tile t-NB (with P over
+          // S also by P_{t-NB}·V, waited for explicitly)
           if (!mbar_wait(k_full(kc % STAGES), (uint32_t)(kc / STAGES) & 1u) ||
-              !mbar_wait(s_free(t & 1), ((uint32_t)(t >> 1) & 1u) ^ 1u)) {
+              !mbar_wait(s_free(sbuf(t)), sph(t) ^ 1u) ||
+              (NB > 2 && t >= NB && !mbar_wait(o_done_of(t - NB), sph(t - NB)))) {
             timed_out = true;
             break;
           }
@@ -694,7 +697,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
         // O holds P_0..P_{j-1}·V of this item relative to m_from: rescale the raised rows
         auto rescale_o = [&](bool raise, float m_from, float m_to) -> bool {
           const float alpha = raise ? ((m_from == -INFINITY) ? 0.f : ex2(m_from - m_to)) : 1.f;
-          const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), sph(t - 1))
+          const bool o_ready = PER_BUF ? mbar_wait(o_done_of(t - 1), sph(t - 1))
                                                   : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
           if (!__all_sync(0xffffffffu, o_ready)) return false;
           tc_fence_after();
@@ -1023,7 +1026,7 @@ fa_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ 
           // and cannot complete P_{t-1+NB}·V (it needs this thread's P), so a
           // parity wait is exact.
           if (j > 0 && __any_sync(0xffffffffu, raise)) {
-            const bool o_ready = KT_FA_ISSUERS == 2 ? mbar_wait(o_done_of(t - 1), sph(t - 1))
+            const bool o_ready = PER_BUF ? mbar_wait(o_done_of(t - 1), sph(t - 1))
                                                     : mbar_wait(o_done, (uint32_t)(t - 1) & 1u);
             if (!__all_sync(0xffffffffu, o_ready)) {
               timed_out = true;

@@ -312,15 +312,15 @@ def is_valid(kernel: str, params: dict) -> bool:
         bn = params.get("bn", 128)
         if (bn // 32) % params.get("psplit", 1):
             return False  # P·V key ranges are whole 32-key chunks
-        if bn == 96 and (not params.get("alt", 0) or params.get("issuers", 2) != 2 or params.get("sbuf", 4) != 4):
-            return False  # 96-key tiles: four S buffers, alternate-tile softmax, two issuers
+        if bn == 96 and (not params.get("alt", 0) or params.get("sbuf", 4) != 4):
+            return False  # 96-key tiles: four S buffers, alternate-tile softmax
         if bn == 128 and params.get("sbuf", 2) == 4:
             return False  # four 128-key S buffers leave no TMEM columns for O
         if params.get("fuse", 0) and not params.get("alt", 0):
             return False  # the fused pass belongs to the alternate-tile softmax
         if params.get("psplit", 1) != 1 and not params.get("alt", 0):
             return False  # the split P·V issue follows the whole-row P stores of the alternate-tile softmax
-        if params.get("sbuf", 2) >= 3 and (params.get("issuers", 2) != 2 or params.get("reload", 0)):
+        if params.get("sbuf", 2) >= 3 and params.get("reload", 0):
             return False  # P over S needs the two issuers and the scores kept in registers
         # head dim 128: two Q buffers + (K + V slots) x 32 KB must fit the 227 KB of shared memory
         return params.get("stages", 2) + params.get("v_stages", 2) <= 4

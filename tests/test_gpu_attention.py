@@ -153,6 +153,8 @@ def test_naive_attention_matches(dev, lib):
     # one speculative pass per tile
     {"kind": 1, "alt": 1, "fuse": 1}, {"kind": 1, "alt": 1, "fuse": 1, "sbuf": 2, "psplit": 1},
     {"kind": 1, "alt": 1, "fuse": 1, "bn": 96},
+    # one issuing thread with P over S (explicit waits for the P·V product that last read a buffer)
+    {"kind": 1, "alt": 1, "issuers": 1, "sbuf": 3}, {"kind": 1, "alt": 0, "issuers": 1, "sbuf": 3},
 ])
 def test_attention_tuning_variants(dev, lib, tmp_path, monkeypatch, params):
     """Kernels of the tuner's attention axes, built as variant libraries: the
