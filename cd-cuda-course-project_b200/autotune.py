@@ -53,7 +53,7 @@ from benchmark import (BenchmarkResult, N_SAMPLES_DEFAULT, N_WARMUP_DEFAULT, _co
                        compute_significance, run_baseline_benchmark)
 from generator import compile_key, ensure_variant  # noqa: E402
 from occupancy import OccupancyAnalyzer  # noqa: E402
-from parser import FAMILIES, build_kernel_profile, build_search_space  # noqa: E402
+from parser import FAMILIES, build_kernel_profile, build_search_space, default_points  # noqa: E402
 from roofline import RooflineAnalyzer  # noqa: E402
 from search import ConvergenceLogger, make_strategy  # noqa: E402
 
@@ -325,7 +325,7 @@ def autotune_kernel(kernel: str, baseline_data: dict, pool: GpuPool, strategy_na
     profile = build_kernel_profile(kernel)
     space = build_search_space(profile)
     strategy = make_strategy(strategy_name, space, kernel=kernel, n_calls=budget or 40,
-                             n_configs=budget or 80, seed=seed)
+                             n_configs=budget or 80, seed=seed, anchors=default_points(kernel, space))
     rdir = results_dir()
     conv = ConvergenceLogger(kernel, rdir)
     roof = RooflineAnalyzer()
@@ -488,7 +488,7 @@ def compile_only(kernels: list[str], strategy_name: str, budget: Optional[int], 
     for k in kernels:
         space = build_search_space(build_kernel_profile(k))
         strategy = make_strategy(strategy_name, space, kernel=k, n_calls=budget or 40, n_configs=budget or 80,
-                                 seed=seed)
+                                 seed=seed, anchors=default_points(k, space))
         pts = strategy.suggest(1 << 30)
         keys = {compile_key(k, p): p for p in pts}
         t0 = time.time()

@@ -327,6 +327,41 @@ def is_valid(kernel: str, params: dict) -> bool:
     return True
 
 
+# The configuration each family's default library (lib/libkt.so) is built with,
+# i.e. the header defaults of the macros generator.MACROS maps the axes to
+# (tests/test_host.py checks the two agree). Axes a kernel ignores carry the
+# representative value is_valid keeps; runtime axes are expanded over their values.
+DEFAULTS: dict[str, list[dict]] = {
+    "softmax": [dict(block_size=256, vec_per_thread=4, min_blocks=1, stages=2, cluster_size=1, tma_box=0)],
+    "layernorm": [dict(block_size=256, vec_per_thread=4, min_blocks=1, stages=2, cluster_size=1, tma_box=0)],
+    "reduction": [dict(block_size=512, unroll=4, blocks_per_sm=4)],
+    "matmul": [dict(variant="tf32", bk=16, ffma_x2=1, ffma_wide=0, min_blocks=2, cta_tile="128x256", stages=4),
+               dict(variant="ffma", bk=8, ffma_x2=0, ffma_wide=1, min_blocks=1, cta_tile="128x128", stages=4)],
+    "attention": [dict(kind=1, stages=2, v_stages=2, poly_exp2=1, issuers=2, alt=1, sbuf=3, x2=1, warp_arrive=0,
+                       spec0=0, dephase=0, psplit=2, bn=128, fuse=0, order=0, poly_every=0)],
+}
+
+
+def default_points(kernel: str, space: dict) -> list[dict]:
+    """The default library's configuration as points of `space` (every value of
+    the runtime axes the defaults leave open), valid ones only. Strategies
+    evaluate these first, so a sweep never reports a winner slower than what it
+    was meant to improve on."""
+    fam = family_of(kernel) if kernel in FAMILIES else kernel
+    keys = [k for k in space if not k.startswith("_")]
+    out: list[dict] = []
+    for base in DEFAULTS.get(fam, []):
+        open_keys = [k for k in keys if k not in base]
+        combos = [{}]
+        for k in open_keys:
+            combos = [dict(c, **{k: v}) for c in combos for v in space[k]]
+        for c in combos:
+            pt = {k: (base[k] if k in base else c[k]) for k in keys}
+            if all(pt[k] in space[k] for k in keys) and is_valid(kernel, pt) and pt not in out:
+                out.append(pt)
+    return out
+
+
 if __name__ == "__main__":
     for fam in FAMILIES:
         prof = build_kernel_profile(fam)

@@ -27,7 +27,7 @@ import math
 import random
 from abc import ABC, abstractmethod
 from pathlib import Path
-from typing import List, Optional
+from typing import List, Optional, Sequence
 
 import numpy as np
 
@@ -134,7 +134,7 @@ class BayesianOptStrategy(SearchStrategy):
     """
 
     def __init__(self, space: dict, kernel: str = "", n_calls: int = 40, n_initial: Optional[int] = None,
-                 length_scale: float = 0.35, noise: float = 1e-3, seed: int = 0) -> None:
+                 length_scale: float = 0.35, noise: float = 1e-3, seed: int = 0, anchors: Sequence[dict] = ()) -> None:
         self._space = space
         self._cands = expand_space(space, kernel)
         self._X = _encode(space, self._cands)
@@ -147,6 +147,8 @@ class BayesianOptStrategy(SearchStrategy):
         self._obs: dict[int, float] = {}
         self._results: list[tuple[dict, float]] = []
         self._index = {_key(p): i for i, p in enumerate(self._cands)}
+        # anchor points (e.g. the default configuration) open the initial design
+        self._anchors = [self._index[_key(p)] for p in anchors if _key(p) in self._index]
 
     def _kernel(self, A: np.ndarray, B: np.ndarray) -> np.ndarray:
         d2 = ((A[:, None, :] - B[None, :, :]) ** 2).sum(-1)
@@ -185,7 +187,10 @@ class BayesianOptStrategy(SearchStrategy):
             free = [i for i in range(len(self._cands)) if i not in self._suggested]
             if not free:
                 break
-            if len(self._obs) < self._n_initial or len(self._suggested) < self._n_initial:
+            pending = [a for a in self._anchors if a not in self._suggested]
+            if pending:
+                i = pending[0]
+            elif len(self._obs) < self._n_initial or len(self._suggested) < self._n_initial:
                 i = self._rng.choice(free)
             else:
                 ei = self.expected_improvement()
@@ -217,10 +222,15 @@ class SuccessiveHalvingStrategy(SearchStrategy):
     """
 
     def __init__(self, space: dict, kernel: str = "", n_configs: int = 80, eta: int = 2, r_min: int = 5,
-                 seed: int = 0) -> None:
+                 seed: int = 0, anchors: Sequence[dict] = ()) -> None:
         cands = expand_space(space, kernel)
         rng = random.Random(seed)
         rng.shuffle(cands)
+        # anchor points (e.g. the default configuration) always enter the first round
+        keys = {_key(p) for p in cands}
+        first = [p for p in anchors if _key(p) in keys]
+        first_keys = {_key(p) for p in first}
+        cands = first + [p for p in cands if _key(p) not in first_keys]
         self._bracket = cands[:min(n_configs, len(cands))]
         self._eta = eta
         self._r_min = r_min
@@ -275,15 +285,16 @@ class SuccessiveHalvingStrategy(SearchStrategy):
 
 
 def make_strategy(name: str, space: dict, kernel: str = "", n_calls: int = 40, n_configs: int = 80,
-                  seed: int = 0) -> SearchStrategy:
-    """'grid' | 'bayesian' | 'sha' (aliases as in the reference)."""
+                  seed: int = 0, anchors: Sequence[dict] = ()) -> SearchStrategy:
+    """'grid' | 'bayesian' | 'sha' (aliases as in the reference). `anchors`:
+    points the sampling strategies evaluate first (the grid visits every point)."""
     name = name.lower()
     if name in ("grid", "gridsearch"):
         return GridSearchStrategy(space, kernel)
     if name in ("bayesian", "bayes", "bo"):
-        return BayesianOptStrategy(space, kernel, n_calls=n_calls, seed=seed)
+        return BayesianOptStrategy(space, kernel, n_calls=n_calls, seed=seed, anchors=anchors)
     if name in ("sha", "successive_halving", "halving"):
-        return SuccessiveHalvingStrategy(space, kernel, n_configs=n_configs, seed=seed)
+        return SuccessiveHalvingStrategy(space, kernel, n_configs=n_configs, seed=seed, anchors=anchors)
     raise ValueError(f"Unknown strategy {name!r}. Choose: grid | bayesian | sha")
 
 

@@ -128,6 +128,47 @@ def test_sha_halves_and_grows_budget():
     assert sha.best() is not None
 
 
+@pytest.mark.parametrize("kernel", list(kparser.FAMILIES))
+def test_default_points_are_the_library_defaults(kernel):
+    """The default library's configuration is a valid point of the family's
+    space, and every axis value of it equals the header default of the macro
+    the axis sets (for the macros whose default is a plain number)."""
+    import re
+    from pathlib import Path
+    space = kparser.build_search_space(kparser.build_kernel_profile(kernel))
+    pts = kparser.default_points(kernel, space)
+    assert pts, kernel
+    csrc = Path(generator.__file__).resolve().parent.parent / "csrc"
+    text = "\n".join(f.read_text() for f in csrc.glob("*.cuh"))
+    fam = kparser.family_of(kernel)
+    for base in kparser.DEFAULTS[fam]:
+        for axis, macro in generator.MACROS[fam].items():
+            if axis not in base:
+                continue
+            if fam == "matmul" and base["variant"] == "tf32" and axis not in ("cta_tile", "stages"):
+                continue  # FFMA-only axes at representative values in the TF32 point
+            if fam == "matmul" and base["variant"] == "ffma" and axis in ("cta_tile", "stages", "bk", "min_blocks"):
+                continue  # tcgen05-only axes; the wide kernel's k tile (8 when bk is unset) and launch
+                          # bounds are its own
+            m = re.search(rf"^#define {macro} (\S+)", text, re.M)
+            assert m, macro
+            if not re.fullmatch(r"-?\d+", m.group(1)):
+                continue  # a derived default (an expression of other macros)
+            assert generator._macro_value(axis, base[axis]) == m.group(1), (axis, macro)
+
+
+def test_strategies_evaluate_anchors_first():
+    sp = {"a": [1, 2, 3, 4], "b": [0, 1, 2, 3]}
+    anchors = [{"a": 3, "b": 2}, {"a": 1, "b": 1}]
+    sha = search.make_strategy("sha", sp, n_configs=4, seed=5, anchors=anchors)
+    assert sha.suggest(2) == anchors
+    bo = search.make_strategy("bayesian", sp, n_calls=6, seed=5, anchors=anchors)
+    assert bo.suggest(2) == anchors
+    # an anchor outside the space is ignored
+    sha = search.make_strategy("sha", sp, n_configs=4, seed=5, anchors=[{"a": 9, "b": 0}])
+    assert {"a": 9, "b": 0} not in sha.suggest(10)
+
+
 def test_make_strategy_names():
     sp = _space()
     assert isinstance(search.make_strategy("grid", sp), search.GridSearchStrategy)
