@@ -43,11 +43,13 @@ constexpr int GROUP_M = 16;  // rasterisation: GROUP_M m-tiles sweep the n-tiles
 
 template <int BN, int STAGES>
 struct Cfg {
-  static_assert(BN == 128 || BN == 256, "BN");
+  // N of the accumulator tile: whole 32-column slabs, at most one 256-column MMA
+  static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256, "BN");
   static constexpr int A_BYTES = BM * BK * 4;
   static constexpr int B_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;
+  // two accumulators; the allocation is a power of two of at least 2·BN columns
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
   static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFFSET + NUM_BARS * 8 + 16 + 1024;

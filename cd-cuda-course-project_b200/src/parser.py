@@ -222,7 +222,7 @@ def build_search_space(profile: KernelProfile) -> dict:
         space["ffma_x2"] = [0, 1]         # ffma: packed fma.rn.f32x2 (two fp32 FMAs per lane per instruction)
         space["ffma_wide"] = [0, 1]       # ffma: 128x256 CTA tile, 8x16 outputs per thread (k tile 8 or 16)
         space["min_blocks"] = [1, 2]      # ffma: resident CTAs per SM asked of the register allocator
-        space["cta_tile"] = ["128x128", "128x256"]
+        space["cta_tile"] = ["128x128", "128x192", "128x224", "128x256"]
         space["stages"] = [3, 4, 5, 6]
     elif fam == "attention":
         space["kind"] = [1, 2]            # 1: one 128-row query tile per CTA; 2: two ping-pong query tiles
@@ -287,8 +287,10 @@ def is_valid(kernel: str, params: dict) -> bool:
                     return False
             return params.get("cta_tile", "128x128") == "128x128" and params.get("stages", 4) == 4
         # the tcgen05 kernel ignores the FFMA axes; a stage holds a 128x32 A box and a BNx32 B box
-        # (48 KB at 128x256), so at most 4 stages of 128x256 fit the 227 KB of shared memory
-        if params.get("cta_tile", "128x128") == "128x256" and params.get("stages", 4) > 4:
+        # (48 KB at 128x256): the 227 KB of shared memory fit 4 stages of 128x256, 5 of 128x192
+        # and 128x224, 6 of 128x128
+        max_stages = {"128x128": 6, "128x192": 5, "128x224": 5, "128x256": 4}[params.get("cta_tile", "128x128")]
+        if params.get("stages", 4) > max_stages:
             return False
         return params.get("bk", 16) == 16 and params.get("ffma_x2", 1) == 1 and params.get("min_blocks", 2) == 2 \
             and params.get("ffma_wide", 0) == 0

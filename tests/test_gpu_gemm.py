@@ -135,6 +135,24 @@ def test_two_variant_libraries_in_one_process(dev, lib, tmp_path, monkeypatch):
             assert ref.normwise_rel_err(C, want) <= 1e-3
 
 
+@pytest.mark.parametrize("tile,stages", [("128x224", 5), ("128x192", 5)])
+def test_gemm_tf32_narrower_tiles(dev, lib, tmp_path, monkeypatch, tile, stages):
+    """TF32 accumulator tiles of 224 and 192 columns with five pipeline stages
+    (tuner axis cta_tile), built as variant libraries: N not a multiple of the
+    tile (a partial last tile), ragged and aligned shapes, both B layouts."""
+    monkeypatch.setenv("KT_RESULTS_DIR", str(tmp_path))
+    import generator
+    ok, log, so = generator.ensure_variant("matmul", {"bk": 16, "cta_tile": tile, "stages": stages})
+    assert ok, log
+    v = kt_lib.KtLibrary(so)
+    for (M, N, K) in ((384, 640, 512), (200, 1000, 96), (1024, 2048, 1024)):
+        inp = workloads.make_inputs("matmul", d={"M": M, "N": N, "K": K}, seed=M + N + K)
+        want = ref.matmul_ref(inp["A"], inp["B"])
+        for tb in (False, True):
+            assert ref.normwise_rel_err(run(v, dev, inp["A"], inp["B"], tb, TF32), want) <= 1e-3
+    assert v.device_error() == 0
+
+
 def test_gemm_ffma_packed_variant(dev, lib, tmp_path, monkeypatch):
     """The packed fma.rn.f32x2 FFMA kernel (tuner axis ffma_x2), built as a
     variant library: exact fp32 like the default, on ragged and aligned shapes."""
